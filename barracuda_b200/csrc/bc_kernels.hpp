@@ -1,0 +1,67 @@
+// bc_kernels.hpp -- host-side launch interface of the CUDA kernels.
+#pragma once
+
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "bc_arith.cuh"
+
+namespace bc {
+
+// Bits OR-ed into the context's device status word by kernels.
+enum : uint32_t {
+    kStatusInputRange = 1u,  // a coefficient >= 2^32 reached a 32-bit-word plan
+};
+
+// Arithmetic flavour of a plan (see bc_arith.cuh).
+enum class Word : int { W32Lazy4 = 0, W32Lazy2 = 1, W64 = 2 };
+
+// Arguments common to the transform kernels.  Strides are in u64 elements.
+struct KArgs {
+    const uint64_t *in;
+    const uint64_t *in2;  // second operand (pointwise, polymul)
+    uint64_t *out;
+    int64_t limb_stride;
+    int64_t poly_stride;
+    uint32_t batch;
+    uint32_t n_limbs;
+    uint32_t logn;
+    uint32_t pad0;
+    const void *tw;      // table used by the (first) transform, N entries per limb
+    const void *tw2;     // table of the second transform (polymul inverse)
+    const LimbConst *limbs;
+    uint32_t *status;    // device status word
+};
+
+// One polynomial per CTA, whole polynomial in shared memory, one stage per
+// barrier.  gs = false: Cooley-Tukey, natural order in, natural order out
+// (bit-reversal applied at the store).  gs = true: Gentleman-Sande, input
+// permuted at the load.  scale_last folds N^-1 into the last stage.
+int launch_ntt_smem(Word w, bool gs, bool scale_last, const KArgs &a, cudaStream_t s);
+// Shared-memory budget of launch_ntt_smem: largest log2 N it accepts.
+uint32_t smem_max_logn(Word w);
+
+// Multi-pass global-memory path for any N (one launch per stage) through a
+// compact scratch buffer of n_limbs * batch * N words of the plan's width.
+int launch_ntt_global(Word w, bool gs, bool scale_last, const KArgs &a, void *scratch,
+                      cudaStream_t s);
+
+// C = A * B mod q per coefficient (exact; inputs < 2^32 for 32-bit words).
+int launch_pointwise(Word w, const KArgs &a, cudaStream_t s);
+// Reference behaviour for modulus 0 (fhe_pointwise_mul.wgsl reduce64 with
+// q = 0 leaves the low 32 bits of the product): C = (A * B) mod 2^32.
+int launch_mul_lo32(const KArgs &a, cudaStream_t s);
+// Fused polymul, one polynomial pair per CTA in shared memory.
+// cyclic: CT(a), CT(b), product, permute, CT(inverse table) with N^-1 folded.
+// negacyclic: CT(a), CT(b), product, GS(inverse table) with N^-1 folded.
+int launch_polymul_smem(Word w, bool cyclic, const KArgs &a, cudaStream_t s);
+uint32_t polymul_smem_max_logn(Word w);
+// Multiplies every coefficient by N^-1 (degree-1 inverse transform).
+int launch_scale(Word w, const KArgs &a, cudaStream_t s);
+
+int launch_fill_uniform(const KArgs &a, uint64_t seed, uint64_t first_poly,
+                        uint64_t total_polys, cudaStream_t s);
+int launch_digest(const uint64_t *in, size_t count, uint64_t *out, cudaStream_t s);
+
+}  // namespace bc

@@ -1,0 +1,376 @@
+// bc_ops.cpp -- the reference op API (validation text, execute semantics)
+// as C++ classes and as the bc_fhe_* C ABI entry points.
+#include "bc_ops.hpp"
+
+#include <cmath>
+
+#include "bc_common.hpp"
+#include "bc_runtime.hpp"
+
+namespace bc {
+const char *last_error_cstr();
+}
+
+using bc::fail;
+using bc::format;
+
+namespace {
+
+// ---- validation, in the order and wording of the Rust constructors ----
+
+// FheNtt::new, crates/barracuda/src/ops/fhe_ntt/mod.rs:95-124.
+int check_ntt(size_t len_u32, uint32_t degree, uint64_t modulus) {
+    const size_t expected = static_cast<size_t>(degree) * 2;
+    if (len_u32 != expected)
+        return fail(BC_ERR_DEVICE, format("Input length %zu doesn't match expected %zu (degree %u * 2)",
+                                          len_u32, expected, degree));
+    if (degree < 2 || !bc::is_pow2(degree))
+        return fail(BC_ERR_DEVICE, format("Degree %u must be a power of 2 \xE2\x89\xA5 2 for NTT", degree));
+    if (modulus == 0) return fail(BC_ERR_DEVICE, "Modulus must be non-zero");
+    if ((modulus - 1) % (2ull * degree) != 0)
+        return fail(BC_ERR_DEVICE,
+                    format("Modulus %llu must satisfy q \xE2\x89\xA1 1 (mod 2N) where N=%u",
+                           static_cast<unsigned long long>(modulus), degree));
+    return BC_OK;
+}
+
+// FheIntt::new, ops/fhe_intt/mod.rs:82-104 (no congruence check, degree 1 allowed).
+int check_intt(size_t len_u32, uint32_t degree, uint64_t modulus) {
+    const size_t expected = static_cast<size_t>(degree) * 2;
+    if (len_u32 != expected)
+        return fail(BC_ERR_DEVICE, format("Input length %zu doesn't match expected %zu (degree %u * 2)",
+                                          len_u32, expected, degree));
+    if (!bc::is_pow2(degree))
+        return fail(BC_ERR_DEVICE, format("Degree %u must be a power of 2 for INTT", degree));
+    if (modulus == 0) return fail(BC_ERR_DEVICE, "Modulus must be non-zero");
+    return BC_OK;
+}
+
+// FhePointwiseMul::new (fhe_pointwise_mul.rs:64-92) and FheFastPolyMul::new
+// (fhe_fast_poly_mul.rs:61-95) share these checks.
+int check_pair(size_t a_len, size_t b_len, uint32_t degree) {
+    if (!bc::is_pow2(degree)) return fail(BC_ERR_DEVICE, format("Degree must be power of 2, got %u", degree));
+    if (degree < 4 || degree > 65536)
+        return fail(BC_ERR_DEVICE, format("Degree must be in range [4, 65_536], got %u", degree));
+    const size_t expected = static_cast<size_t>(degree) * 2;
+    if (a_len != expected)
+        return fail(BC_ERR_DEVICE,
+                    format("Input A has wrong length: expected %zu, got %zu", expected, a_len));
+    if (b_len != expected)
+        return fail(BC_ERR_DEVICE,
+                    format("Input B has wrong length: expected %zu, got %zu", expected, b_len));
+    return BC_OK;
+}
+
+// Moduli the CUDA path cannot represent (>= 2^62): the reference accepts
+// them but computes truncated products there.
+int check_width(uint64_t modulus) {
+    if (modulus >= (1ull << 62))
+        return fail(BC_ERR_UNSUPPORTED,
+                    format("modulus %llu is >= 2^62; the CUDA path supports moduli below 2^62",
+                           static_cast<unsigned long long>(modulus)));
+    return BC_OK;
+}
+
+int run_ntt(bc_ctx *ctx, const uint64_t *in, uint32_t degree, uint64_t modulus, uint64_t root,
+            uint64_t *out) {
+    int st = check_width(modulus);
+    if (st) return st;
+    bc_plan *p = nullptr;
+    if ((st = bc::cached_plan(ctx, degree, modulus, root, 0, BC_NTT_CYCLIC, &p))) return st;
+    if ((st = bc::run_forward(p, in, out, 1, nullptr, ctx->stream))) return st;
+    return bc::ctx_sync(ctx);
+}
+
+int run_intt(bc_ctx *ctx, const uint64_t *in, uint32_t degree, uint64_t modulus, uint64_t inv_root,
+             uint64_t *out) {
+    int st = check_width(modulus);
+    if (st) return st;
+    bc_plan *p = nullptr;
+    // cyclic plan whose inverse table is built from inv_root
+    if ((st = bc::cached_plan(ctx, degree, modulus, 0, inv_root, BC_NTT_CYCLIC, &p))) return st;
+    if ((st = bc::run_inverse(p, in, out, 1, nullptr, ctx->stream))) return st;
+    return bc::ctx_sync(ctx);
+}
+
+int run_pointwise(bc_ctx *ctx, const uint64_t *a, const uint64_t *b, uint32_t degree,
+                  uint64_t modulus, uint64_t *out) {
+    int st;
+    if (modulus == 0) {
+        // The reference constructor accepts q = 0 and its shader then keeps
+        // the low 32 bits of each product (fhe_pointwise_mul.wgsl:70-95).
+        if ((st = bc::use_device(ctx))) return st;
+        bc::KArgs k = {};
+        k.in = a;
+        k.in2 = b;
+        k.out = out;
+        k.poly_stride = degree;
+        k.limb_stride = degree;
+        k.batch = 1;
+        k.n_limbs = 1;
+        k.logn = bc::ilog2(degree);
+        k.status = ctx->d_status;
+        if ((st = bc::launch_mul_lo32(k, ctx->stream))) return st;
+        return bc::ctx_sync(ctx);
+    }
+    if ((st = check_width(modulus))) return st;
+    bc_plan *p = nullptr;
+    if ((st = bc::cached_plan(ctx, degree, modulus, 0, 0, BC_NTT_CYCLIC, &p))) return st;
+    if ((st = bc::run_pointwise(p, a, b, out, 1, nullptr, ctx->stream))) return st;
+    return bc::ctx_sync(ctx);
+}
+
+int run_fast_poly_mul(bc_ctx *ctx, const uint64_t *a, const uint64_t *b, uint32_t degree,
+                      uint64_t modulus, uint64_t root, uint64_t *out) {
+    // execute() builds FheNtt for both inputs first (fhe_fast_poly_mul.rs:124-139),
+    // so the NTT constructor's modulus checks apply here.
+    int st = check_ntt(static_cast<size_t>(degree) * 2, degree, modulus);
+    if (st) return st;
+    if ((st = check_width(modulus))) return st;
+    const uint64_t inv_root = bc::ref_fastmul_modinv(root, modulus);
+    bc_plan *p = nullptr;
+    if ((st = bc::cached_plan(ctx, degree, modulus, root, inv_root, BC_NTT_CYCLIC, &p))) return st;
+    if ((st = bc::run_polymul(p, a, b, out, 1, nullptr, ctx->stream))) return st;
+    return bc::ctx_sync(ctx);
+}
+
+}  // namespace
+
+// ================================================================ C++ API
+
+namespace barracuda {
+
+namespace {
+Error last(int st) { return Error{st, bc::last_error_cstr()}; }
+}  // namespace
+
+std::string Error::to_string() const {
+    switch (kind) {
+    case BC_ERR_DEVICE: return "Device error: " + message;
+    case BC_ERR_INVALID_INPUT: return "Invalid input: " + message;
+    case BC_ERR_OUT_OF_MEMORY: return "Out of memory: " + message;
+    case BC_ERR_DEVICE_LOST: return "GPU device lost: " + message;
+    case BC_ERR_GPU: return "GPU error: " + message;
+    case BC_ERR_UNSUPPORTED: return "Operation not supported on device: " + message;
+    case BC_ERR_DEVICE_NOT_AVAILABLE: return "Device not available: " + message;
+    case BC_ERR_EXECUTION: return "Execution error: " + message;
+    case BC_ERR_INTERNAL: return "Internal error: " + message;
+    default: return message;
+    }
+}
+
+Result<std::shared_ptr<Device>> Device::open(int ordinal) {
+    bc_ctx *c = nullptr;
+    const int st = bc_ctx_create(ordinal, &c);
+    if (st) return Result<std::shared_ptr<Device>>::err(last(st));
+    return Result<std::shared_ptr<Device>>::ok(std::shared_ptr<Device>(new Device(c)));
+}
+
+Device::~Device() { bc_ctx_destroy(ctx_); }
+
+Result<Tensor> Tensor::empty_u64(size_t n_u64, std::shared_ptr<Device> dev) {
+    void *p = nullptr;
+    const int st = bc_buf_alloc(dev->ctx(), n_u64 * 8, &p);
+    if (st) return Result<Tensor>::err(last(st));
+    Tensor t;
+    bc_ctx *c = dev->ctx();
+    t.dev_ = dev;
+    t.buf_ = std::shared_ptr<void>(p, [dev](void *q) { bc_buf_free(dev->ctx(), q); });
+    t.len_u32_ = n_u64 * 2;
+    (void)c;
+    return Result<Tensor>::ok(std::move(t));
+}
+
+Result<Tensor> Tensor::from_u32(const std::vector<uint32_t> &data, std::shared_ptr<Device> dev) {
+    auto r = empty_u64((data.size() + 1) / 2, dev);
+    if (r.is_err()) return r;
+    Tensor t = r.take();
+    t.len_u32_ = data.size();
+    const int st = bc_buf_h2d(dev->ctx(), t.mutable_data(), data.data(), data.size() * 4);
+    if (st) return Result<Tensor>::err(last(st));
+    return Result<Tensor>::ok(std::move(t));
+}
+
+Result<std::vector<uint32_t>> Tensor::to_vec_u32() const {
+    std::vector<uint32_t> out(len_u32_);
+    const int st = bc_buf_d2h(dev_->ctx(), out.data(), buf_.get(), len_u32_ * 4);
+    if (st) return Result<std::vector<uint32_t>>::err(last(st));
+    return Result<std::vector<uint32_t>>::ok(std::move(out));
+}
+
+Result<Tensor> create_fhe_poly_tensor(const std::vector<uint64_t> &poly, std::shared_ptr<Device> dev) {
+    std::vector<uint32_t> words;
+    words.reserve(poly.size() * 2);
+    for (uint64_t v : poly) {
+        words.push_back(static_cast<uint32_t>(v));
+        words.push_back(static_cast<uint32_t>(v >> 32));
+    }
+    return Tensor::from_u32(words, std::move(dev));
+}
+
+uint64_t compute_primitive_root(uint32_t degree, uint64_t modulus) {
+    return bc_compute_primitive_root(degree, modulus);
+}
+
+uint64_t compute_inverse_root(uint32_t degree, uint64_t modulus, uint64_t root) {
+    return bc_compute_inverse_root(degree, modulus, root);
+}
+
+Result<FheNtt> FheNtt::create(Tensor input, uint32_t degree, uint64_t modulus, uint64_t root) {
+    const int st = check_ntt(input.len(), degree, modulus);
+    if (st) return Result<FheNtt>::err(last(st));
+    FheNtt op;
+    op.input_ = std::move(input);
+    op.degree_ = degree;
+    op.modulus_ = modulus;
+    op.root_ = root;
+    return Result<FheNtt>::ok(std::move(op));
+}
+
+Result<Tensor> FheNtt::execute() && {
+    auto out = Tensor::empty_u64(degree_, input_.device());
+    if (out.is_err()) return out;
+    const int st = run_ntt(input_.device()->ctx(), input_.data(), degree_, modulus_, root_,
+                           out.value().mutable_data());
+    if (st) return Result<Tensor>::err(last(st));
+    return out;
+}
+
+Result<FheIntt> FheIntt::create(Tensor input, uint32_t degree, uint64_t modulus, uint64_t inv_root) {
+    const int st = check_intt(input.len(), degree, modulus);
+    if (st) return Result<FheIntt>::err(last(st));
+    FheIntt op;
+    op.input_ = std::move(input);
+    op.degree_ = degree;
+    op.modulus_ = modulus;
+    op.inv_root_ = inv_root;
+    return Result<FheIntt>::ok(std::move(op));
+}
+
+Result<Tensor> FheIntt::execute() && {
+    auto out = Tensor::empty_u64(degree_, input_.device());
+    if (out.is_err()) return out;
+    const int st = run_intt(input_.device()->ctx(), input_.data(), degree_, modulus_, inv_root_,
+                            out.value().mutable_data());
+    if (st) return Result<Tensor>::err(last(st));
+    return out;
+}
+
+Result<FhePointwiseMul> FhePointwiseMul::create(Tensor a, Tensor b, uint32_t degree, uint64_t modulus) {
+    int st = check_pair(a.len(), b.len(), degree);
+    if (!st && a.device() != b.device())
+        st = fail(BC_ERR_DEVICE, "input_a and input_b must be on the same device");
+    if (st) return Result<FhePointwiseMul>::err(last(st));
+    FhePointwiseMul op;
+    op.a_ = std::move(a);
+    op.b_ = std::move(b);
+    op.degree_ = degree;
+    op.modulus_ = modulus;
+    return Result<FhePointwiseMul>::ok(std::move(op));
+}
+
+Result<Tensor> FhePointwiseMul::execute() const {
+    auto out = Tensor::empty_u64(degree_, a_.device());
+    if (out.is_err()) return out;
+    const int st = run_pointwise(a_.device()->ctx(), a_.data(), b_.data(), degree_, modulus_,
+                                 out.value().mutable_data());
+    if (st) return Result<Tensor>::err(last(st));
+    return out;
+}
+
+Result<FheFastPolyMul> FheFastPolyMul::create(Tensor a, Tensor b, uint32_t degree, uint64_t modulus,
+                                              uint64_t root) {
+    const int st = check_pair(a.len(), b.len(), degree);
+    if (st) return Result<FheFastPolyMul>::err(last(st));
+    FheFastPolyMul op;
+    op.a_ = std::move(a);
+    op.b_ = std::move(b);
+    op.degree_ = degree;
+    op.modulus_ = modulus;
+    op.root_ = root;
+    return Result<FheFastPolyMul>::ok(std::move(op));
+}
+
+Result<Tensor> FheFastPolyMul::execute() const {
+    auto out = Tensor::empty_u64(degree_, a_.device());
+    if (out.is_err()) return out;
+    const int st = run_fast_poly_mul(a_.device()->ctx(), a_.data(), b_.data(), degree_, modulus_,
+                                     root_, out.value().mutable_data());
+    if (st) return Result<Tensor>::err(last(st));
+    return out;
+}
+
+// fhe_fast_poly_mul.rs:160-170: N / log2 N times the 16.4% efficiency the
+// reference measured for its own path.
+double FheFastPolyMul::expected_speedup() const {
+    const double n = static_cast<double>(degree_);
+    return n / std::log2(n) * 0.164;
+}
+
+}  // namespace barracuda
+
+// ================================================================== C ABI
+
+extern "C" {
+
+uint64_t bc_compute_primitive_root(uint32_t degree, uint64_t modulus) {
+    return bc::ref_primitive_root(degree, modulus);
+}
+
+uint64_t bc_compute_inverse_root(uint32_t degree, uint64_t modulus, uint64_t root) {
+    (void)degree;
+    return bc::ref_modinv(root, modulus);
+}
+
+int bc_fhe_ntt_check(size_t input_len_u32, uint32_t degree, uint64_t modulus, uint64_t root) {
+    (void)root;
+    return check_ntt(input_len_u32, degree, modulus);
+}
+
+int bc_fhe_ntt(bc_ctx *ctx, const uint64_t *d_in, size_t input_len_u32, uint32_t degree,
+               uint64_t modulus, uint64_t root, uint64_t *d_out) {
+    if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
+    const int st = check_ntt(input_len_u32, degree, modulus);
+    return st ? st : run_ntt(ctx, d_in, degree, modulus, root, d_out);
+}
+
+int bc_fhe_intt_check(size_t input_len_u32, uint32_t degree, uint64_t modulus, uint64_t inv_root) {
+    (void)inv_root;
+    return check_intt(input_len_u32, degree, modulus);
+}
+
+int bc_fhe_intt(bc_ctx *ctx, const uint64_t *d_in, size_t input_len_u32, uint32_t degree,
+                uint64_t modulus, uint64_t inv_root, uint64_t *d_out) {
+    if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
+    const int st = check_intt(input_len_u32, degree, modulus);
+    return st ? st : run_intt(ctx, d_in, degree, modulus, inv_root, d_out);
+}
+
+int bc_fhe_pointwise_mul_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree, uint64_t modulus) {
+    (void)modulus;
+    return check_pair(a_len_u32, b_len_u32, degree);
+}
+
+int bc_fhe_pointwise_mul(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const uint64_t *d_b,
+                         size_t b_len_u32, uint32_t degree, uint64_t modulus, uint64_t *d_out) {
+    if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
+    const int st = check_pair(a_len_u32, b_len_u32, degree);
+    return st ? st : run_pointwise(ctx, d_a, d_b, degree, modulus, d_out);
+}
+
+int bc_fhe_fast_poly_mul_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree, uint64_t modulus,
+                               uint64_t root) {
+    (void)modulus;
+    (void)root;
+    return check_pair(a_len_u32, b_len_u32, degree);
+}
+
+int bc_fhe_fast_poly_mul(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const uint64_t *d_b,
+                         size_t b_len_u32, uint32_t degree, uint64_t modulus, uint64_t root,
+                         uint64_t *d_out) {
+    if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
+    const int st = check_pair(a_len_u32, b_len_u32, degree);
+    return st ? st : run_fast_poly_mul(ctx, d_a, d_b, degree, modulus, root, d_out);
+}
+
+}  // extern "C"

@@ -1,0 +1,676 @@
+// bc_runtime.cpp -- contexts, device buffers, plans (twiddle tables), the
+// batched transform entry points and the multi-GPU split of the C ABI.
+#include "bc_runtime.hpp"
+
+#include <algorithm>
+#include <cstring>
+#include <thread>
+
+namespace bc {
+const char *last_error_cstr();
+
+int cuda_fail(cudaError_t e, const char *what) {
+    int st = BC_ERR_GPU;
+    switch (e) {
+    case cudaErrorMemoryAllocation: st = BC_ERR_OUT_OF_MEMORY; break;
+    case cudaErrorNoDevice:
+    case cudaErrorInvalidDevice:
+    case cudaErrorInsufficientDriver: st = BC_ERR_DEVICE_NOT_AVAILABLE; break;
+    case cudaErrorIllegalAddress:
+    case cudaErrorLaunchFailure:
+    case cudaErrorIllegalInstruction:
+    case cudaErrorMisalignedAddress:
+    case cudaErrorHardwareStackError:
+    case cudaErrorECCUncorrectable:
+    case cudaErrorDevicesUnavailable: st = BC_ERR_DEVICE_LOST; break;
+    default: break;
+    }
+    return fail(st, format("%s: %s", what, cudaGetErrorString(e)));
+}
+
+int use_device(const bc_ctx *ctx) {
+    const cudaError_t e = cudaSetDevice(ctx->device);
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "cudaSetDevice");
+}
+
+int ctx_sync(bc_ctx *ctx) {
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+    uint32_t st = 0;
+    e = cudaMemcpy(&st, ctx->d_status, sizeof st, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "status readback");
+    if (st) {
+        cudaMemset(ctx->d_status, 0, sizeof st);
+        if (st & kStatusInputRange)
+            return fail(BC_ERR_INVALID_INPUT,
+                        "coefficient >= 2^32 given to a transform whose moduli are below 2^31 "
+                        "(inputs must be reduced; the reference is exact only below 2^32)");
+        return fail(BC_ERR_EXECUTION, format("kernel reported status 0x%x", st));
+    }
+    return BC_OK;
+}
+
+// ---------------------------------------------------------------- tables
+
+namespace {
+
+Word choose_word(const std::vector<uint64_t> &moduli) {
+    uint64_t mx = 0;
+    for (uint64_t q : moduli) mx = std::max(mx, q);
+    if (mx < (1ull << 30)) return Word::W32Lazy4;
+    if (mx < (1ull << 31)) return Word::W32Lazy2;
+    return Word::W64;
+}
+
+bool is32(Word w) { return w != Word::W64; }
+
+// Powers base^0 .. base^(count-1) mod q by repeated multiplication (the
+// same sequence as compute_twiddle_factors, fhe_ntt/mod.rs:174-184).
+std::vector<uint64_t> powers(uint64_t base, uint64_t q, uint32_t count) {
+    std::vector<uint64_t> out(count);
+    uint64_t p = 1 % q;
+    for (uint32_t k = 0; k < count; ++k) {
+        out[k] = p;
+        p = mulmod(p, base, q);
+    }
+    return out;
+}
+
+uint32_t floor_log2(uint32_t k) {
+    uint32_t l = 0;
+    while ((k >> (l + 1)) != 0) ++l;
+    return l;
+}
+
+// Twiddle value (no Shoup companion) of entry k in [1, N) of one table.
+struct TableGen {
+    uint32_t L = 0, N = 0;
+    int mode = BC_NTT_CYCLIC;
+    bool inverse = false;
+    uint64_t q = 0, ninv = 0;
+    std::vector<uint64_t> pw;  // powers of the table's base root
+
+    void init(uint32_t logn, int md, bool inv, uint64_t modulus, uint64_t root, uint64_t inv_root,
+              uint64_t n_inverse) {
+        L = logn;
+        N = 1u << logn;
+        mode = md;
+        inverse = inv;
+        q = modulus;
+        ninv = n_inverse;
+        if (mode == BC_NTT_CYCLIC) {
+            // CT-ordered DIT network: entry m + i (m = 2^s) is
+            // r^(bitrev_s(i) * N / (2m)); exponents < N/2.
+            pw = powers((inverse ? inv_root : root) % q, q, std::max(N / 2, 1u));
+        } else {
+            // negacyclic: psi^(+-bitrev_L(k)); exponents < N.
+            pw = powers((inverse ? inv_root : root) % q, q, N);
+        }
+    }
+
+    uint64_t value(uint32_t k) const {
+        if (k == 0 || k >= N) return 0;
+        uint64_t w;
+        if (mode == BC_NTT_CYCLIC) {
+            const uint32_t s = floor_log2(k);
+            const uint32_t m = 1u << s, i = k - m;
+            w = pw[static_cast<size_t>(s ? bitrev(i, s) : 0) * (N / (2 * m))];
+            // last CT stage of the inverse (m = N/2) carries N^-1
+            if (inverse && m == N / 2) w = mulmod(w, ninv, q);
+        } else {
+            w = pw[bitrev(k, L)];
+            // last GS stage (m = 1) carries N^-1
+            if (inverse && k == 1) w = mulmod(w, ninv, q);
+        }
+        return w % q;
+    }
+};
+
+}  // namespace
+
+int plan_build_host(bc_plan &p, uint32_t degree, uint32_t n_limbs, const uint64_t *moduli,
+                    const uint64_t *roots, const uint64_t *inv_roots, int mode,
+                    std::vector<unsigned char> *fwd, std::vector<unsigned char> *inv) {
+    if (degree == 0 || !is_pow2(degree))
+        return fail(BC_ERR_INVALID_INPUT, format("degree %u must be a power of two", degree));
+    if (n_limbs == 0) return fail(BC_ERR_INVALID_INPUT, "n_limbs must be at least 1");
+    if (!moduli || !roots) return fail(BC_ERR_INVALID_INPUT, "moduli and roots must not be NULL");
+    if (mode != BC_NTT_CYCLIC && mode != BC_NTT_NEGACYCLIC)
+        return fail(BC_ERR_INVALID_INPUT, format("unknown transform mode %d", mode));
+    if (mode == BC_NTT_NEGACYCLIC && inv_roots)
+        return fail(BC_ERR_INVALID_INPUT, "negacyclic plans derive the inverse root; pass NULL");
+    if (degree > (1u << 24))
+        return fail(BC_ERR_UNSUPPORTED, format("degree %u above 2^24 is not supported", degree));
+    p.degree = degree;
+    p.logn = ilog2(degree);
+    p.n_limbs = n_limbs;
+    p.mode = mode;
+    p.moduli.assign(moduli, moduli + n_limbs);
+    p.roots.assign(roots, roots + n_limbs);
+    p.inv_roots.resize(n_limbs);
+    for (uint32_t l = 0; l < n_limbs; ++l) {
+        const uint64_t q = moduli[l];
+        if (q == 0) return fail(BC_ERR_INVALID_INPUT, format("modulus of limb %u is zero", l));
+        if (q >= (1ull << 62))
+            return fail(BC_ERR_UNSUPPORTED,
+                        format("modulus %llu of limb %u is >= 2^62 (largest supported width)",
+                               static_cast<unsigned long long>(q), l));
+        if (mode == BC_NTT_NEGACYCLIC) {
+            if (q < 3 || (q - 1) % (2ull * degree) != 0)
+                return fail(BC_ERR_INVALID_INPUT,
+                            format("modulus %llu of limb %u must satisfy q == 1 (mod 2N), N=%u",
+                                   static_cast<unsigned long long>(q), l, degree));
+            if (powmod(roots[l] % q, degree, q) != q - 1)
+                return fail(BC_ERR_INVALID_INPUT,
+                            format("root %llu of limb %u is not a primitive 2N-th root of unity "
+                                   "mod %llu (psi^N must be -1)",
+                                   static_cast<unsigned long long>(roots[l]), l,
+                                   static_cast<unsigned long long>(q)));
+            p.inv_roots[l] = ref_modinv(roots[l] % q, q);
+        } else {
+            p.inv_roots[l] = inv_roots ? inv_roots[l] : ref_modinv(roots[l], q);
+        }
+    }
+    p.word = choose_word(p.moduli);
+    const bool w32 = is32(p.word);
+    p.limbs.resize(n_limbs);
+    const uint32_t N = degree;
+    const size_t entry = w32 ? 8 : 16;
+    if (fwd) fwd->assign(entry * N * n_limbs, 0);
+    if (inv) inv->assign(entry * N * n_limbs, 0);
+    for (uint32_t l = 0; l < n_limbs; ++l) {
+        const uint64_t q = p.moduli[l];
+        LimbConst &c = p.limbs[l];
+        std::memset(&c, 0, sizeof c);
+        c.q = q;
+        const uint64_t ninv = ref_modinv(degree, q) % q;
+        c.ninv = ninv;
+        if (w32) {
+            c.one_shoup = q == 1 ? 0xFFFFFFFFull : (1ull << 32) / q;
+            c.ninv_shoup = shoup32(static_cast<uint32_t>(ninv), static_cast<uint32_t>(q));
+            c.barrett = q == 1 ? ~0ull
+                               : static_cast<uint64_t>((static_cast<unsigned __int128>(1) << 64) / q);
+        } else {
+            c.one_shoup = shoup64(1, q);
+            c.ninv_shoup = shoup64(ninv, q);
+            const uint32_t k = 64 - static_cast<uint32_t>(__builtin_clzll(q));
+            c.bk = k;
+            c.barrett = static_cast<uint64_t>((static_cast<unsigned __int128>(1) << (2 * k)) / q);
+        }
+        for (int t = 0; t < 2; ++t) {
+            std::vector<unsigned char> *dst = t == 0 ? fwd : inv;
+            if (!dst) continue;
+            TableGen g;
+            g.init(p.logn, mode, t == 1, q, p.roots[l], p.inv_roots[l], ninv);
+            unsigned char *base = dst->data() + entry * static_cast<size_t>(N) * l;
+            for (uint32_t k = 1; k < N; ++k) {
+                const uint64_t w = g.value(k);
+                if (w32) {
+                    uint32_t pair[2] = {static_cast<uint32_t>(w),
+                                        shoup32(static_cast<uint32_t>(w), static_cast<uint32_t>(q))};
+                    std::memcpy(base + entry * k, pair, 8);
+                } else {
+                    uint64_t pair[2] = {w, shoup64(w, q)};
+                    std::memcpy(base + entry * k, pair, 16);
+                }
+            }
+        }
+    }
+    p.table_bytes = 2ull * entry * N * n_limbs;
+    if (p.logn == 0)
+        p.kind = KernelKind::Scale;
+    else if (p.logn <= smem_max_logn(p.word))
+        p.kind = KernelKind::Smem;
+    else
+        p.kind = KernelKind::Global;
+    return BC_OK;
+}
+
+void table_entry(const bc_plan &p, uint32_t limb, int table, uint32_t k, uint64_t *w,
+                 uint64_t *wq) {
+    TableGen g;
+    g.init(p.logn, p.mode, table == 1, p.moduli[limb], p.roots[limb], p.inv_roots[limb],
+           p.limbs[limb].ninv);
+    const uint64_t v = g.value(k);
+    *w = v;
+    *wq = is32(p.word) ? shoup32(static_cast<uint32_t>(v), static_cast<uint32_t>(p.moduli[limb]))
+                       : shoup64(v, p.moduli[limb]);
+}
+
+// ---------------------------------------------------------------- launches
+
+namespace {
+
+int make_args(bc_plan *p, const uint64_t *in, const uint64_t *in2, uint64_t *out,
+              uint32_t batch, const bc_layout *layout, KArgs *a) {
+    if (batch == 0) return fail(BC_ERR_INVALID_INPUT, "batch must be at least 1");
+    if ((!in && batch) || !out) return fail(BC_ERR_INVALID_INPUT, "device pointers must not be NULL");
+    std::memset(a, 0, sizeof *a);
+    a->in = in;
+    a->in2 = in2;
+    a->out = out;
+    a->poly_stride = layout ? layout->poly_stride : p->degree;
+    a->limb_stride = layout ? layout->limb_stride : static_cast<int64_t>(batch) * p->degree;
+    if (layout && (layout->poly_stride < 0 || layout->limb_stride < 0))
+        return fail(BC_ERR_INVALID_INPUT, "layout strides must be non-negative");
+    a->batch = batch;
+    a->n_limbs = p->n_limbs;
+    a->logn = p->logn;
+    a->limbs = p->d_limbs;
+    a->status = p->ctx->d_status;
+    return BC_OK;
+}
+
+int ensure_scratch(bc_plan *p, size_t bytes, cudaStream_t s) {
+    std::lock_guard<std::mutex> lk(p->scratch_mu);
+    if (p->scratch_bytes >= bytes) return BC_OK;
+    if (p->d_scratch) {
+        cudaStreamSynchronize(s);
+        cudaFree(p->d_scratch);
+        p->d_scratch = nullptr;
+        p->scratch_bytes = 0;
+    }
+    const cudaError_t e = cudaMalloc(&p->d_scratch, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "scratch allocation");
+    p->scratch_bytes = bytes;
+    return BC_OK;
+}
+
+size_t wbytes(Word w) { return w == Word::W64 ? 8 : 4; }
+
+int run_transform(bc_plan *p, bool inverse, const uint64_t *in, uint64_t *out, uint32_t batch,
+                  const bc_layout *layout, cudaStream_t s) {
+    KArgs a;
+    int st = make_args(p, in, nullptr, out, batch, layout, &a);
+    if (st) return st;
+    if ((st = use_device(p->ctx))) return st;
+    const bool gs = inverse && p->mode == BC_NTT_NEGACYCLIC;
+    a.tw = inverse ? p->d_tw_inv : p->d_tw_fwd;
+    switch (p->kind) {
+    case KernelKind::Scale:
+        // degree 1: both directions multiply by N^-1 = 1 (reduction mod q)
+        return launch_scale(p->word, a, s);
+    case KernelKind::Smem: return launch_ntt_smem(p->word, gs, inverse, a, s);
+    default: {
+        const size_t need = wbytes(p->word) * (static_cast<size_t>(batch) * p->n_limbs) << p->logn;
+        if ((st = ensure_scratch(p, need, s))) return st;
+        return launch_ntt_global(p->word, gs, inverse, a, p->d_scratch, s);
+    }
+    }
+}
+
+}  // namespace
+
+int run_forward(bc_plan *p, const uint64_t *in, uint64_t *out, uint32_t batch,
+                const bc_layout *layout, cudaStream_t s) {
+    return run_transform(p, false, in, out, batch, layout, s);
+}
+
+int run_inverse(bc_plan *p, const uint64_t *in, uint64_t *out, uint32_t batch,
+                const bc_layout *layout, cudaStream_t s) {
+    return run_transform(p, true, in, out, batch, layout, s);
+}
+
+int run_pointwise(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t *c, uint32_t batch,
+                  const bc_layout *layout, cudaStream_t s) {
+    KArgs a;
+    int st = make_args(p, a_, b, c, batch, layout, &a);
+    if (st) return st;
+    if (!b) return fail(BC_ERR_INVALID_INPUT, "device pointers must not be NULL");
+    if ((st = use_device(p->ctx))) return st;
+    return launch_pointwise(p->word, a, s);
+}
+
+int run_polymul(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t *c, uint32_t batch,
+                const bc_layout *layout, cudaStream_t s) {
+    KArgs a;
+    int st = make_args(p, a_, b, c, batch, layout, &a);
+    if (st) return st;
+    if (!b) return fail(BC_ERR_INVALID_INPUT, "device pointers must not be NULL");
+    if ((st = use_device(p->ctx))) return st;
+    const bool cyclic = p->mode == BC_NTT_CYCLIC;
+    if (p->logn >= 1 && p->logn <= polymul_smem_max_logn(p->word)) {
+        a.tw = p->d_tw_fwd;
+        a.tw2 = p->d_tw_inv;
+        return launch_polymul_smem(p->word, cyclic, a, s);
+    }
+    // Unfused fallback above the fused size: forward both operands into a
+    // temporary compact buffer, multiply, inverse into the caller's layout.
+    const bool caller_compact =
+        !layout || (layout->poly_stride == p->degree &&
+                    layout->limb_stride == static_cast<int64_t>(batch) * p->degree);
+    if (!caller_compact)
+        return fail(BC_ERR_UNSUPPORTED, "polymul above the fused size needs the default layout");
+    const size_t words = (static_cast<size_t>(batch) * p->n_limbs) << p->logn;
+    uint64_t *tmp = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, 2 * words * sizeof(uint64_t));
+    if (e != cudaSuccess) return cuda_fail(e, "polymul scratch allocation");
+    int r = run_transform(p, false, a_, tmp, batch, layout, s);
+    if (!r) r = run_transform(p, false, b, tmp + words, batch, layout, s);
+    if (!r) r = run_pointwise(p, tmp, tmp + words, tmp, batch, layout, s);
+    if (!r) r = run_transform(p, true, tmp, c, batch, layout, s);
+    cudaStreamSynchronize(s);
+    cudaFree(tmp);
+    return r;
+}
+
+int cached_plan(bc_ctx *ctx, uint32_t degree, uint64_t modulus, uint64_t root, uint64_t inv_root,
+                int mode, bc_plan **out) {
+    std::lock_guard<std::mutex> lk(ctx->cache_mu);
+    for (auto it = ctx->cache.begin(); it != ctx->cache.end(); ++it) {
+        if (it->degree == degree && it->modulus == modulus && it->root == root &&
+            it->inv_root == inv_root && it->mode == mode) {
+            ctx->cache.splice(ctx->cache.begin(), ctx->cache, it);
+            *out = it->plan;
+            return BC_OK;
+        }
+    }
+    bc_plan *p = nullptr;
+    const int st = bc_plan_create(ctx, degree, 1, &modulus, &root,
+                                  mode == BC_NTT_CYCLIC ? &inv_root : nullptr, mode, &p);
+    if (st) return st;
+    ctx->cache.push_front({degree, modulus, root, inv_root, mode, p});
+    while (ctx->cache.size() > 32) {
+        bc_plan_destroy(ctx->cache.back().plan);
+        ctx->cache.pop_back();
+    }
+    *out = p;
+    return BC_OK;
+}
+
+}  // namespace bc
+
+using namespace bc;
+
+// ================================================================== C ABI
+
+extern "C" {
+
+const char *bc_last_error(void) { return bc::last_error_cstr(); }
+
+int bc_abi_version(void) { return BC_ABI_VERSION; }
+
+int bc_device_count(int *count) {
+    if (!count) return fail(BC_ERR_INVALID_INPUT, "count must not be NULL");
+    int n = 0;
+    const cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        *count = 0;
+        return cuda_fail(e, "cudaGetDeviceCount");
+    }
+    *count = n;
+    return BC_OK;
+}
+
+int bc_ctx_create(int device, bc_ctx **out) {
+    if (!out) return fail(BC_ERR_INVALID_INPUT, "out must not be NULL");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= n)
+        return fail(BC_ERR_DEVICE_NOT_AVAILABLE, format("device %d not present (%d visible)", device, n));
+    if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    cudaDeviceProp prop;
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess)
+        return cuda_fail(e, "cudaGetDeviceProperties");
+    if (prop.major != 10)
+        return fail(BC_ERR_UNSUPPORTED,
+                    format("device %d is sm_%d%d; this library is built for sm_100a (B200)", device,
+                           prop.major, prop.minor));
+    auto *c = new bc_ctx();
+    c->device = device;
+    if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "cudaStreamCreate");
+    }
+    if ((e = cudaMalloc(&c->d_status, sizeof(uint32_t))) != cudaSuccess ||
+        (e = cudaMemset(c->d_status, 0, sizeof(uint32_t))) != cudaSuccess) {
+        cudaStreamDestroy(c->stream);
+        delete c;
+        return cuda_fail(e, "status word allocation");
+    }
+    *out = c;
+    return BC_OK;
+}
+
+int bc_ctx_destroy(bc_ctx *ctx) {
+    if (!ctx) return BC_OK;
+    use_device(ctx);
+    cudaStreamSynchronize(ctx->stream);
+    for (auto &e : ctx->cache) bc_plan_destroy(e.plan);
+    ctx->cache.clear();
+    cudaFree(ctx->d_status);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return BC_OK;
+}
+
+int bc_ctx_device(const bc_ctx *ctx, int *device) {
+    if (!ctx || !device) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    *device = ctx->device;
+    return BC_OK;
+}
+
+int bc_ctx_stream(bc_ctx *ctx, void **stream) {
+    if (!ctx || !stream) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    *stream = ctx->stream;
+    return BC_OK;
+}
+
+int bc_ctx_sync(bc_ctx *ctx) {
+    if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
+    int st = use_device(ctx);
+    return st ? st : ctx_sync(ctx);
+}
+
+int bc_buf_alloc(bc_ctx *ctx, size_t bytes, void **dptr) {
+    if (!ctx || !dptr) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    *dptr = nullptr;
+    int st = use_device(ctx);
+    if (st) return st;
+    const cudaError_t e = cudaMalloc(dptr, bytes ? bytes : 1);
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "cudaMalloc");
+}
+
+int bc_buf_free(bc_ctx *ctx, void *dptr) {
+    if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
+    if (!dptr) return BC_OK;
+    use_device(ctx);
+    const cudaError_t e = cudaFree(dptr);
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "cudaFree");
+}
+
+static int copy_sync(bc_ctx *ctx, void *dst, const void *src, size_t bytes, cudaMemcpyKind k) {
+    if (!ctx || (!dst && bytes) || (!src && bytes)) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    int st = use_device(ctx);
+    if (st) return st;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, k, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "cudaMemcpy");
+}
+
+int bc_buf_h2d(bc_ctx *ctx, void *dst, const void *src, size_t bytes) {
+    return copy_sync(ctx, dst, src, bytes, cudaMemcpyHostToDevice);
+}
+
+int bc_buf_d2h(bc_ctx *ctx, void *dst, const void *src, size_t bytes) {
+    return copy_sync(ctx, dst, src, bytes, cudaMemcpyDeviceToHost);
+}
+
+static int copy_async(bc_ctx *ctx, void *dst, const void *src, size_t bytes, cudaMemcpyKind k,
+                      void *stream) {
+    if (!ctx || (!dst && bytes) || (!src && bytes)) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    int st = use_device(ctx);
+    if (st) return st;
+    const cudaError_t e =
+        cudaMemcpyAsync(dst, src, bytes, k, stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "cudaMemcpyAsync");
+}
+
+int bc_buf_h2d_async(bc_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream) {
+    return copy_async(ctx, dst, src, bytes, cudaMemcpyHostToDevice, stream);
+}
+
+int bc_buf_d2h_async(bc_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream) {
+    return copy_async(ctx, dst, src, bytes, cudaMemcpyDeviceToHost, stream);
+}
+
+int bc_host_alloc(size_t bytes, void **hptr) {
+    if (!hptr) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    const cudaError_t e = cudaMallocHost(hptr, bytes ? bytes : 1);
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "cudaMallocHost");
+}
+
+int bc_host_free(void *hptr) {
+    if (!hptr) return BC_OK;
+    const cudaError_t e = cudaFreeHost(hptr);
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "cudaFreeHost");
+}
+
+int bc_plan_create(bc_ctx *ctx, uint32_t degree, uint32_t n_limbs, const uint64_t *moduli,
+                   const uint64_t *roots, const uint64_t *inv_roots, int mode, bc_plan **out) {
+    if (!ctx || !out) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    *out = nullptr;
+    auto *p = new bc_plan();
+    p->ctx = ctx;
+    std::vector<unsigned char> fwd, inv;
+    int st = plan_build_host(*p, degree, n_limbs, moduli, roots, inv_roots, mode, &fwd, &inv);
+    if (st) {
+        delete p;
+        return st;
+    }
+    if ((st = use_device(ctx))) {
+        delete p;
+        return st;
+    }
+    cudaError_t e = cudaMalloc(&p->d_limbs, sizeof(LimbConst) * n_limbs);
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_tw_fwd, fwd.size());
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_tw_inv, inv.size());
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(p->d_limbs, p->limbs.data(), sizeof(LimbConst) * n_limbs,
+                            cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(p->d_tw_fwd, fwd.data(), fwd.size(), cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(p->d_tw_inv, inv.data(), inv.size(), cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        st = cuda_fail(e, "plan upload");
+        bc_plan_destroy(p);
+        return st;
+    }
+    *out = p;
+    return BC_OK;
+}
+
+int bc_plan_destroy(bc_plan *p) {
+    if (!p) return BC_OK;
+    use_device(p->ctx);
+    cudaStreamSynchronize(p->ctx->stream);
+    cudaFree(p->d_limbs);
+    cudaFree(p->d_tw_fwd);
+    cudaFree(p->d_tw_inv);
+    cudaFree(p->d_scratch);
+    delete p;
+    return BC_OK;
+}
+
+int bc_plan_info_get(const bc_plan *p, bc_plan_info *out) {
+    if (!p || !out) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    out->degree = p->degree;
+    out->n_limbs = p->n_limbs;
+    out->mode = p->mode;
+    out->word_bits = p->word == Word::W64 ? 64 : 32;
+    out->kernel_kind = static_cast<int32_t>(p->kind);
+    out->cluster_size = p->cluster;
+    out->table_bytes = p->table_bytes;
+    return BC_OK;
+}
+
+static cudaStream_t pick_stream(bc_plan *p, void *stream) {
+    return stream ? static_cast<cudaStream_t>(stream) : p->ctx->stream;
+}
+
+int bc_ntt_forward(bc_plan *p, const uint64_t *in, uint64_t *out, uint32_t batch,
+                   const bc_layout *layout, void *stream) {
+    if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");
+    return run_forward(p, in, out, batch, layout, pick_stream(p, stream));
+}
+
+int bc_ntt_inverse(bc_plan *p, const uint64_t *in, uint64_t *out, uint32_t batch,
+                   const bc_layout *layout, void *stream) {
+    if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");
+    return run_inverse(p, in, out, batch, layout, pick_stream(p, stream));
+}
+
+int bc_pointwise_mul(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t batch,
+                     const bc_layout *layout, void *stream) {
+    if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");
+    return run_pointwise(p, a, b, c, batch, layout, pick_stream(p, stream));
+}
+
+int bc_polymul(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t batch,
+               const bc_layout *layout, void *stream) {
+    if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");
+    return run_polymul(p, a, b, c, batch, layout, pick_stream(p, stream));
+}
+
+int bc_fill_uniform(bc_plan *p, uint64_t *out, uint32_t batch, const bc_layout *layout, uint64_t seed,
+                    uint64_t first_poly, uint64_t total_polys, void *stream) {
+    if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");
+    KArgs a;
+    std::memset(&a, 0, sizeof a);
+    if (!out || batch == 0) return fail(BC_ERR_INVALID_INPUT, "empty fill");
+    a.out = out;
+    a.poly_stride = layout ? layout->poly_stride : p->degree;
+    a.limb_stride = layout ? layout->limb_stride : static_cast<int64_t>(batch) * p->degree;
+    a.batch = batch;
+    a.n_limbs = p->n_limbs;
+    a.logn = p->logn;
+    a.limbs = p->d_limbs;
+    int st = use_device(p->ctx);
+    if (st) return st;
+    return launch_fill_uniform(a, seed, first_poly, total_polys, pick_stream(p, stream));
+}
+
+int bc_digest(bc_ctx *ctx, const uint64_t *in, size_t count, uint64_t *out, void *stream) {
+    if (!ctx || !out || (!in && count)) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    int st = use_device(ctx);
+    if (st) return st;
+    return launch_digest(in, count, out, stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
+}
+
+int bc_partition(uint64_t units, uint32_t shards, uint32_t shard, uint64_t *begin, uint64_t *count) {
+    if (!begin || !count) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    if (shards == 0 || shard >= shards)
+        return fail(BC_ERR_INVALID_INPUT, format("shard %u out of range for %u shards", shard, shards));
+    const uint64_t base = units / shards, extra = units % shards;
+    *count = base + (shard < extra ? 1 : 0);
+    *begin = shard * base + (shard < extra ? shard : extra);
+    return BC_OK;
+}
+
+uint64_t bc_ntt_prime(uint32_t bits, uint32_t degree, uint32_t index) {
+    return ntt_prime(bits, degree, index);
+}
+
+uint64_t bc_negacyclic_root(uint64_t modulus, uint32_t degree) {
+    if (modulus < 3 || degree == 0 || (modulus - 1) % (2ull * degree) != 0 || !is_prime(modulus)) return 0;
+    const uint64_t g = smallest_generator(modulus);
+    return powmod(g, (modulus - 1) / (2ull * degree), modulus);
+}
+
+int bc_debug_twiddle(uint32_t degree, uint64_t modulus, uint64_t root, uint64_t inv_root, int mode,
+                     int table, uint32_t k, uint64_t *w, uint64_t *w_shoup) {
+    if (!w || !w_shoup) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    bc_plan p;
+    int st = plan_build_host(p, degree, 1, &modulus, &root,
+                             mode == BC_NTT_CYCLIC ? &inv_root : nullptr, mode, nullptr, nullptr);
+    if (st) return st;
+    if (k == 0 || k >= degree) return fail(BC_ERR_INVALID_INPUT, "entry index out of range");
+    table_entry(p, 0, table, k, w, w_shoup);
+    return BC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,81 @@
+// bc_runtime.hpp -- contexts and plans behind the C ABI.
+#pragma once
+
+#include <cstdint>
+#include <list>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "bc_common.hpp"
+#include "bc_kernels.hpp"
+
+struct bc_plan;
+
+// One per GPU: a stream, a device status word and a cache of plans used by
+// the single-polynomial reference-op entry points.
+struct bc_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    uint32_t *d_status = nullptr;
+    std::mutex cache_mu;
+    struct CacheEntry {
+        uint32_t degree;
+        uint64_t modulus, root, inv_root;
+        int mode;
+        bc_plan *plan;
+    };
+    std::list<CacheEntry> cache;  // most recent first
+};
+
+enum class KernelKind : int { Smem = 0, Cluster = 1, Global = 2, Scale = 3 };
+
+struct bc_plan {
+    bc_ctx *ctx = nullptr;
+    uint32_t degree = 0, logn = 0, n_limbs = 0;
+    int mode = BC_NTT_CYCLIC;
+    bc::Word word = bc::Word::W64;
+    KernelKind kind = KernelKind::Smem;
+    int cluster = 1;
+    std::vector<uint64_t> moduli, roots, inv_roots;
+    std::vector<bc::LimbConst> limbs;
+    bc::LimbConst *d_limbs = nullptr;
+    void *d_tw_fwd = nullptr;  // forward CT table
+    void *d_tw_inv = nullptr;  // inverse table (CT for cyclic, GS for negacyclic), N^-1 folded
+    uint64_t table_bytes = 0;
+    std::mutex scratch_mu;
+    void *d_scratch = nullptr;
+    size_t scratch_bytes = 0;
+};
+
+namespace bc {
+
+// Sets the device of `ctx` current on the calling thread.
+int use_device(const bc_ctx *ctx);
+// Maps a CUDA error to a status (and records the message).
+int cuda_fail(cudaError_t e, const char *what);
+// Host-side table entry (w, w') of limb `limb`; table 0 forward, 1 inverse.
+void table_entry(const bc_plan &p, uint32_t limb, int table, uint32_t k, uint64_t *w,
+                 uint64_t *wq);
+// Builds limb constants and tables on the host (no device work).
+int plan_build_host(bc_plan &p, uint32_t degree, uint32_t n_limbs, const uint64_t *moduli,
+                    const uint64_t *roots, const uint64_t *inv_roots, int mode,
+                    std::vector<unsigned char> *fwd, std::vector<unsigned char> *inv);
+// Plan for the reference-op entry points, cached per context.
+int cached_plan(bc_ctx *ctx, uint32_t degree, uint64_t modulus, uint64_t root,
+                uint64_t inv_root, int mode, bc_plan **out);
+// Waits for the context stream and converts kernel status bits to errors.
+int ctx_sync(bc_ctx *ctx);
+
+int run_forward(bc_plan *p, const uint64_t *in, uint64_t *out, uint32_t batch,
+                const bc_layout *layout, cudaStream_t s);
+int run_inverse(bc_plan *p, const uint64_t *in, uint64_t *out, uint32_t batch,
+                const bc_layout *layout, cudaStream_t s);
+int run_pointwise(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c,
+                  uint32_t batch, const bc_layout *layout, cudaStream_t s);
+int run_polymul(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c,
+                uint32_t batch, const bc_layout *layout, cudaStream_t s);
+
+}  // namespace bc

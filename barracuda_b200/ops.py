@@ -1,0 +1,213 @@
+"""Python mirror of barraCuda's FHE op API (crates/barracuda/src/ops/fhe_*.rs).
+
+Same names, constructor arguments, validation (order and message text) and
+execute semantics as the Rust ops; everything runs through the C ABI of
+libbarracuda_fhe.so, so these classes are what a parity test written like the
+reference's own tests calls::
+
+    dev = Device(0)
+    t = create_fhe_poly_tensor([1, 2, 3, 4], dev)
+    out = FheNtt.new(t, 4, 17, 4).execute()      # tests/fhe/ntt.rs style
+    assert read_poly_from_tensor(out) == [10, 7, 15, 6]
+
+``FheNtt.new`` raises BarracudaError exactly where ``FheNtt::new`` returns Err.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Iterable, Sequence
+
+import numpy as np
+
+from . import _native as N
+from ._native import BarracudaError, check, lib
+
+__all__ = [
+    "BarracudaError", "Device", "FheTensor", "create_fhe_poly_tensor", "read_poly_from_tensor",
+    "compute_primitive_root", "compute_inverse_root", "FheNtt", "FheIntt", "FhePointwiseMul",
+    "FheFastPolyMul",
+]
+
+
+class Device:
+    """One GPU (the role WgpuDevice plays for this path): a bc_ctx and its stream."""
+
+    def __init__(self, ordinal: int = 0):
+        h = ctypes.c_void_p()
+        check(lib().bc_ctx_create(ordinal, ctypes.byref(h)))
+        self.handle = h
+        self.ordinal = ordinal
+
+    def stream(self) -> int:
+        s = ctypes.c_void_p()
+        check(lib().bc_ctx_stream(self.handle, ctypes.byref(s)))
+        return s.value or 0
+
+    def synchronize(self) -> None:
+        check(lib().bc_ctx_sync(self.handle))
+
+    def close(self) -> None:
+        if self.handle:
+            lib().bc_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class FheTensor:
+    """Device buffer of u32 words: ``len()`` counts u32 words like Tensor::len()."""
+
+    def __init__(self, device: Device, n_u32: int):
+        self.device = device
+        self._len = int(n_u32)
+        p = ctypes.c_void_p()
+        check(lib().bc_buf_alloc(device.handle, max(8, (self._len + 1) // 2 * 8), ctypes.byref(p)))
+        self.ptr = p.value
+
+    def len(self) -> int:
+        return self._len
+
+    def __len__(self) -> int:
+        return self._len
+
+    @classmethod
+    def from_u32(cls, words: np.ndarray, device: Device) -> "FheTensor":
+        words = np.ascontiguousarray(np.asarray(words, dtype=np.uint32))
+        t = cls(device, words.size)
+        if words.size:
+            check(lib().bc_buf_h2d(device.handle, t.ptr, words.ctypes.data, words.nbytes))
+        return t
+
+    def to_vec_u32(self) -> np.ndarray:
+        out = np.zeros(self._len, dtype=np.uint32)
+        if self._len:
+            check(lib().bc_buf_d2h(self.device.handle, out.ctypes.data, self.ptr, out.nbytes))
+        return out
+
+    def to_u64(self) -> np.ndarray:
+        return self.to_vec_u32().view(np.uint64) if self._len % 2 == 0 else \
+            np.frombuffer(np.append(self.to_vec_u32(), np.uint32(0)).tobytes(), dtype=np.uint64)
+
+    def free(self) -> None:
+        if self.ptr:
+            lib().bc_buf_free(self.device.handle, self.ptr)
+            self.ptr = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            if self.device.handle:
+                self.free()
+        except Exception:
+            pass
+
+
+def create_fhe_poly_tensor(poly: Iterable[int], device: Device) -> FheTensor:
+    """ops/fhe_poly_add.rs:185: u64 coefficients -> [lo32, hi32] u32 words."""
+    arr = np.ascontiguousarray(np.asarray(list(poly) if not isinstance(poly, np.ndarray) else poly,
+                                          dtype=np.uint64))
+    return FheTensor.from_u32(arr.view(np.uint32), device)
+
+
+def read_poly_from_tensor(t: FheTensor) -> list:
+    """tests/fhe/helpers.rs:110-127: u32 pairs -> u64 coefficients."""
+    return [int(v) for v in t.to_u64()]
+
+
+def compute_primitive_root(degree: int, modulus: int) -> int:
+    """ops/fhe_ntt/mod.rs:210-242."""
+    return int(lib().bc_compute_primitive_root(degree, modulus))
+
+
+def compute_inverse_root(degree: int, modulus: int, root: int) -> int:
+    """ops/fhe_intt/mod.rs:202-204."""
+    return int(lib().bc_compute_inverse_root(degree, modulus, root))
+
+
+class FheNtt:
+    """ops/fhe_ntt/mod.rs:71-171; execute() is compute.rs:29-143 (consumes the op)."""
+
+    def __init__(self, input: FheTensor, degree: int, modulus: int, root_of_unity: int):
+        check(lib().bc_fhe_ntt_check(input.len(), degree, modulus, root_of_unity))
+        self.input, self.degree, self.modulus, self.root_of_unity = input, degree, modulus, root_of_unity
+
+    @classmethod
+    def new(cls, input, degree, modulus, root_of_unity) -> "FheNtt":
+        return cls(input, degree, modulus, root_of_unity)
+
+    def execute(self) -> FheTensor:
+        out = FheTensor(self.input.device, 2 * self.degree)
+        check(lib().bc_fhe_ntt(self.input.device.handle, self.input.ptr, self.input.len(),
+                               self.degree, self.modulus, self.root_of_unity, out.ptr))
+        return out
+
+
+class FheIntt:
+    """ops/fhe_intt/mod.rs:58-160; execute() is compute.rs:27-168."""
+
+    def __init__(self, input: FheTensor, degree: int, modulus: int, inv_root_of_unity: int):
+        check(lib().bc_fhe_intt_check(input.len(), degree, modulus, inv_root_of_unity))
+        self.input, self.degree, self.modulus = input, degree, modulus
+        self.inv_root_of_unity = inv_root_of_unity
+
+    @classmethod
+    def new(cls, input, degree, modulus, inv_root_of_unity) -> "FheIntt":
+        return cls(input, degree, modulus, inv_root_of_unity)
+
+    def execute(self) -> FheTensor:
+        out = FheTensor(self.input.device, 2 * self.degree)
+        check(lib().bc_fhe_intt(self.input.device.handle, self.input.ptr, self.input.len(),
+                                self.degree, self.modulus, self.inv_root_of_unity, out.ptr))
+        return out
+
+
+class FhePointwiseMul:
+    """ops/fhe_pointwise_mul.rs:34-156."""
+
+    def __init__(self, input_a: FheTensor, input_b: FheTensor, degree: int, modulus: int):
+        check(lib().bc_fhe_pointwise_mul_check(input_a.len(), input_b.len(), degree, modulus))
+        if input_a.device is not input_b.device:
+            raise BarracudaError(N.BC_ERR_DEVICE, "input_a and input_b must be on the same device")
+        self.input_a, self.input_b, self.degree, self.modulus = input_a, input_b, degree, modulus
+
+    @classmethod
+    def new(cls, input_a, input_b, degree, modulus) -> "FhePointwiseMul":
+        return cls(input_a, input_b, degree, modulus)
+
+    def execute(self) -> FheTensor:
+        out = FheTensor(self.input_a.device, 2 * self.degree)
+        check(lib().bc_fhe_pointwise_mul(self.input_a.device.handle, self.input_a.ptr,
+                                         self.input_a.len(), self.input_b.ptr, self.input_b.len(),
+                                         self.degree, self.modulus, out.ptr))
+        return out
+
+
+class FheFastPolyMul:
+    """ops/fhe_fast_poly_mul.rs:39-171; execute() runs one fused kernel."""
+
+    def __init__(self, input_a: FheTensor, input_b: FheTensor, degree: int, modulus: int,
+                 root_of_unity: int):
+        check(lib().bc_fhe_fast_poly_mul_check(input_a.len(), input_b.len(), degree, modulus,
+                                               root_of_unity))
+        self.input_a, self.input_b, self.degree = input_a, input_b, degree
+        self.modulus, self.root_of_unity = modulus, root_of_unity
+
+    @classmethod
+    def new(cls, input_a, input_b, degree, modulus, root_of_unity) -> "FheFastPolyMul":
+        return cls(input_a, input_b, degree, modulus, root_of_unity)
+
+    def execute(self) -> FheTensor:
+        out = FheTensor(self.input_a.device, 2 * self.degree)
+        check(lib().bc_fhe_fast_poly_mul(self.input_a.device.handle, self.input_a.ptr,
+                                         self.input_a.len(), self.input_b.ptr, self.input_b.len(),
+                                         self.degree, self.modulus, self.root_of_unity, out.ptr))
+        return out
+
+    def expected_speedup(self) -> float:
+        """fhe_fast_poly_mul.rs:160-170."""
+        n = float(self.degree)
+        return n / math.log2(n) * 0.164

@@ -1,0 +1,377 @@
+"""Benchmark of the FHE NTT hot path (negacyclic NTT + INTT at N = 2^16).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: N = 2^16, 48 RNS limbs (the 48 largest primes
+below 2^31 with q = 1 mod 2N: the reference is exact only below 2^31),
+128 ciphertexts x 2 polynomials per GPU, layout [ct][2][limb][N] (u64), seeded
+uniform coefficients.  One step = one forward negacyclic NTT and one INTT of
+every limb-polynomial (24,576 limb-transforms per GPU).  Each GPU owns its own
+contiguous range of ciphertexts (no collective on the data path), so per-GPU
+work is fixed as GPUs are added ("weak" scaling); --strong splits 128
+ciphertexts over the GPUs instead.  Inputs (6.4 GB per GPU) are larger than
+L2, so no flush is needed between steps.
+
+Metric: limb-transforms/s for the whole job (all GPUs), device time from CUDA
+events on the launching stream, max over ranks.  `e2e` repeats the step through
+the public API with host buffers: pinned host -> device copy of the inputs,
+forward + inverse, device -> host copy of the results, chunked over streams.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_LOG = 16
+N = 1 << N_LOG
+LIMBS = 48
+CTS_PER_GPU = 128
+BYTES_PER_TRANSFORM = 16 * N        # read N u64 + write N u64 (algorithmic)
+METRIC = "negacyclic NTT limb-transforms/s at N=2^16 (fwd+inv, 48 limbs, 128 ct x 2 polys per GPU)"
+UNIT = "limb-transforms/s"
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant
+# kernel, from the ncu capture summarised in profiles/ (None until captured).
+NCU_TRAFFIC_PER_TRANSFORM = None
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[1].isdigit():
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace('.', '', 1).isdigit())
+                if any(r[3].replace('.', '', 1).isdigit() for r in rows) else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# --------------------------------------------------------------- reference arm
+
+def run_reference(args):
+    """The reference's own algorithm on the host cores (oracle port of the WGSL
+    path: bit-serial u64 emulation, radix-2 DIT passes, separate scale pass),
+    negacyclic via the reference's own ops (pointwise twist + cyclic NTT)."""
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    q = [oracle.ntt_prime(31, N, i) for i in range(LIMBS)]
+    psi = [oracle.psi(x, N) for x in q]
+    per_step = threads  # limb-polys per step: one per host thread (fwd + inv each)
+    x = np.concatenate([oracle.seeded_fill(N, 0, p * N, q[p % LIMBS]) for p in range(per_step)])
+    times = []
+    for it in range(args.warmup + args.steps):
+        t_f, X = oracle.baseline_run("negacyclic_ntt", x, N, q[:per_step], psi[:per_step], threads)
+        t_i, y = oracle.baseline_run("negacyclic_intt", X, N, q[:per_step], psi[:per_step], threads)
+        if it >= args.warmup:
+            times.append(t_f + t_i)
+        assert (y == x).all()
+    total = sum(times)
+    value = 2 * per_step * len(times) / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u32 (u64 storage)",
+        "data": "synthetic",
+        "config": {"workload": f"config3 sample: {per_step} limb-polys of N=2^16 per step (fwd+inv), "
+                               "q < 2^31, reference algorithm restated in C (oracle/ref_wgsl.c)",
+                   "N": N, "limbs": LIMBS},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{per_step} limb-polys x (fwd+inv) per step, {args.steps} steps"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_sample(seconds_target=12.0):
+    """Oracle (reference algorithm) timed on the host cores on a bounded sample."""
+    import numpy as np
+    from oracle import oracle
+    threads = os.cpu_count() or 1
+    q = [oracle.ntt_prime(31, N, i) for i in range(LIMBS)]
+    psi = [oracle.psi(x, N) for x in q]
+    # calibrate with one polynomial per thread, then scale to ~seconds_target
+    count = threads
+    x = np.concatenate([oracle.seeded_fill(N, 0, p * N, q[p % LIMBS]) for p in range(count)])
+    t, _ = oracle.baseline_run("negacyclic_ntt", x, N, q[:count], psi[:count], threads)
+    reps = max(1, int(seconds_target / max(t, 1e-3) / 2))
+    count = min(threads * reps, 4 * LIMBS * 8)
+    x = np.concatenate([oracle.seeded_fill(N, 0, p * N, q[p % LIMBS]) for p in range(count)])
+    qq = [q[p % LIMBS] for p in range(count)]
+    pp = [psi[p % LIMBS] for p in range(count)]
+    t_f, X = oracle.baseline_run("negacyclic_ntt", x, N, qq, pp, threads)
+    t_i, _ = oracle.baseline_run("negacyclic_intt", X, N, qq, pp, threads)
+    return {"value": 2 * count / (t_f + t_i), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{count} limb-polys of N=2^16, fwd+inv, reference algorithm (oracle/ref_wgsl.c), "
+                      f"{t_f + t_i:.1f} s"}
+
+
+# --------------------------------------------------------------- our arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import barracuda_b200 as bc
+
+    world, rank, local = dist_setup()
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = bc.Device(local)
+
+    cts_total = args.cts_total if args.strong else CTS_PER_GPU * world
+    ct_begin, ct_count = bc.partition(cts_total, world, rank)
+    polys = 2 * ct_count
+    qs = bc.ntt_primes(31, N, LIMBS)
+    psis = [bc.negacyclic_root(q, N) for q in qs]
+    plan = bc.NttPlan(dev, N, qs, psis, mode=bc.NEGACYCLIC)
+    lay = bc.Layout(limb_stride=N, poly_stride=LIMBS * N)
+    words = polys * LIMBS * N
+    x = torch.empty(words, dtype=torch.int64, device="cuda")
+    X = torch.empty(words, dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    plan.fill_uniform(x, polys, seed=0, first_poly=2 * ct_begin, total_polys=2 * cts_total,
+                      layout=lay, stream=sh)
+    dig = torch.zeros(2, dtype=torch.int64, device="cuda")
+    bc.digest(dev, x, words, dig[0:1], stream=sh)
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        plan.forward(x, X, polys, layout=lay, stream=sh)
+        if ev is not None:
+            ev[1].record(stream)
+        plan.inverse(X, x, polys, layout=lay, stream=sh)
+        if ev is not None:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for k in range(args.steps):
+        step(evs[k])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    inv_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    units = torch.tensor([2.0 * polys * LIMBS * args.steps], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(units, op=dist.ReduceOp.SUM)
+    ms_max = float(t.item())
+    value = float(units.item()) / (ms_max / 1000.0)
+
+    # round trip must leave the inputs unchanged
+    bc.digest(dev, x, words, dig[1:2], stream=sh)
+    torch.cuda.synchronize()
+    roundtrip_ok = bool(dig[0].item() == dig[1].item())
+
+    # ---- e2e through the public API with pinned host buffers
+    e2e = run_e2e(args, torch, bc, dev, plan, lay, polys, words, qs, x, X, rank, world, dist)
+
+    info = plan.info
+    launches_per_transform = {0: 1, 1: 1, 2: N_LOG + 2, 3: 1}[info["kernel_kind"]]
+    hbm, peak_kind = peaks()
+    per_launch_bytes = BYTES_PER_TRANSFORM * polys * LIMBS
+    fwd_avg = statistics.mean(fwd_ms)
+    inv_avg = statistics.mean(inv_ms)
+    achieved = per_launch_bytes / (fwd_avg / 1000.0) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_kind": peak_kind,
+                "kernel": "negacyclic forward NTT (one launch over all limb-polys of the GPU)",
+                "algorithmic_bytes_per_launch": per_launch_bytes,
+                "avg_launch_ms": fwd_avg, "inverse_avg_launch_ms": inv_avg,
+                "traffic": (NCU_TRAFFIC_PER_TRANSFORM * polys * LIMBS
+                            if NCU_TRAFFIC_PER_TRANSFORM else None)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+            "dtype": "u32 (u64 storage)", "data": "synthetic",
+            "config": {"workload": "config3: N=2^16 negacyclic NTT+INTT, 48 limbs (largest primes "
+                                   "< 2^31, q = 1 mod 2N), [ct][2][limb][N] u64 layout",
+                       "cts_per_gpu": ct_count, "cts_total": cts_total, "limb_transforms_per_step":
+                       int(units.item() / args.steps), "l2": "inputs 6.4 GB/GPU > 126 MB L2, no flush",
+                       "parallelism": f"shard by ciphertext x{world}",
+                       "kernel_kind": info["kernel_kind"], "cluster": info["cluster_size"]},
+            "gb_per_s": value * BYTES_PER_TRANSFORM / 1e9,
+            "roofline": roofline,
+            "clocks": clk,
+            "gpu_launches": 2 * launches_per_transform * args.steps,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "roundtrip_identity": roundtrip_ok,
+        }
+        print(json.dumps(line), flush=True)
+    plan.close()
+    dev.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(args, torch, bc, dev, plan, lay, polys, words, qs, x, X, rank, world, dist):
+    """Host buffers in, host buffers out, through the same public calls."""
+    steps = max(1, min(args.steps, args.e2e_steps))
+    host = torch.empty(words, dtype=torch.int64, pin_memory=True)
+    # inputs for e2e: the seeded data, staged once to pinned host memory
+    host.copy_(x, non_blocking=False)
+    chunks = max(1, args.e2e_chunks)
+    cts = polys // 2
+    streams = [torch.cuda.Stream() for _ in range(2)]
+    per = [(c * cts) // chunks for c in range(chunks + 1)]
+    elem_per_ct = 2 * LIMBS * N
+
+    def one_step():
+        cur = torch.cuda.current_stream()
+        for s in streams:
+            s.wait_stream(cur)
+        for c in range(chunks):
+            s = streams[c % 2]
+            lo, hi = per[c] * elem_per_ct, per[c + 1] * elem_per_ct
+            if hi == lo:
+                continue
+            npol = 2 * (per[c + 1] - per[c])
+            with torch.cuda.stream(s):
+                x[lo:hi].copy_(host[lo:hi], non_blocking=True)
+                plan.forward(x[lo:hi], X[lo:hi], npol, layout=lay, stream=s.cuda_stream)
+                plan.inverse(X[lo:hi], x[lo:hi], npol, layout=lay, stream=s.cuda_stream)
+                host[lo:hi].copy_(x[lo:hi], non_blocking=True)
+
+    one_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        one_step()
+        for s in streams:
+            torch.cuda.current_stream().wait_stream(s)
+    ev1.record()
+    torch.cuda.synchronize()
+    secs = ev0.elapsed_time(ev1) / 1000.0
+    t = torch.tensor([secs], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    units = 2.0 * polys * LIMBS * steps * world
+    return {"value": units / float(t.item()), "unit": UNIT,
+            "h2d_bytes_per_step": words * 8, "d2h_bytes_per_step": words * 8,
+            "steps": steps, "chunks": chunks,
+            "timing": "CUDA events around the copy/compute streams, max over ranks"}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--strong", action="store_true", help="split 128 ciphertexts over the GPUs")
+    ap.add_argument("--cts-total", type=int, default=CTS_PER_GPU)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-chunks", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,221 @@
+/*
+ * barracuda_fhe.h -- C ABI of the B200-native FHE NTT path.
+ *
+ * The shared library libbarracuda_fhe.so implements barraCuda's FHE hot path
+ * (forward NTT, inverse INTT, pointwise modular multiply, NTT-based
+ * polynomial product) with hand-written sm_100a CUDA kernels.  The ABI uses
+ * plain pointers, sizes and integer status codes only, so that a thin Rust
+ * crate (barracuda-cuda-sys) can bind it with `extern "C"` declarations and
+ * keep every `unsafe` block in that one crate.
+ *
+ * Reference interfaces replaced (paths inside ecoPrimals/barraCuda):
+ *   - crates/barracuda/src/ops/fhe_ntt/mod.rs:95 FheNtt::new,
+ *     fhe_ntt/compute.rs:29 FheNtt::execute                 -> bc_fhe_ntt*
+ *   - ops/fhe_intt/mod.rs:82 FheIntt::new, compute.rs:27     -> bc_fhe_intt*
+ *   - ops/fhe_pointwise_mul.rs:64,119 FhePointwiseMul        -> bc_fhe_pointwise_mul*
+ *   - ops/fhe_fast_poly_mul.rs:61,122 FheFastPolyMul         -> bc_fhe_fast_poly_mul*
+ *   - ops/fhe_ntt/mod.rs:210 compute_primitive_root          -> bc_compute_primitive_root
+ *   - ops/fhe_intt/mod.rs:202 compute_inverse_root           -> bc_compute_inverse_root
+ *   - ops/fhe_poly_add.rs:185 create_fhe_poly_tensor,
+ *     tensor/mod.rs:197 Tensor::from_data_pod, :456 to_vec_u32 -> bc_buf_*
+ *   - device/backend.rs:311 GpuBackend::dispatch_compute (the per-stage
+ *     dispatch the ops issue today)                         -> bc_ntt_* on a plan
+ *   - multi_gpu/gpu_pool.rs:194 GpuPool::parallel_map (nearest analog of the
+ *     shard split)                                          -> bc_partition
+ *
+ * Data layout: a polynomial of degree N is N little-endian uint64_t
+ * coefficients in natural order, byte-identical to the reference's
+ * [lo32, hi32] u32-pair tensors (Tensor::len() == 2N u32 words).
+ *
+ * Errors: every call returns a bc_status; on failure a message is kept per
+ * thread and returned by bc_last_error().  Status codes map one to one onto
+ * BarracudaError variants (crates/barracuda/src/error.rs).
+ *
+ * Threading: one bc_ctx per GPU.  A bc_plan is immutable after creation and
+ * may be shared by threads; launches on one stream are ordered.
+ */
+#ifndef BARRACUDA_FHE_H
+#define BARRACUDA_FHE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BC_ABI_VERSION 1
+
+typedef enum bc_status {
+    BC_OK = 0,
+    BC_ERR_DEVICE = 1,               /* BarracudaError::Device(String), error.rs:20 (op validation) */
+    BC_ERR_INVALID_INPUT = 2,        /* BarracudaError::InvalidInput, error.rs:80 */
+    BC_ERR_OUT_OF_MEMORY = 3,        /* BarracudaError::OutOfMemory, error.rs:67 */
+    BC_ERR_DEVICE_LOST = 4,          /* BarracudaError::DeviceLost, error.rs:59 */
+    BC_ERR_GPU = 5,                  /* BarracudaError::Gpu, error.rs:50 */
+    BC_ERR_UNSUPPORTED = 6,          /* BarracudaError::UnsupportedOperation, error.rs:71 */
+    BC_ERR_DEVICE_NOT_AVAILABLE = 7, /* BarracudaError::DeviceNotAvailable, error.rs:93 */
+    BC_ERR_EXECUTION = 8,            /* BarracudaError::ExecutionError, error.rs:86 */
+    BC_ERR_INTERNAL = 9              /* BarracudaError::Internal, error.rs:108 */
+} bc_status;
+
+typedef struct bc_ctx bc_ctx;
+typedef struct bc_plan bc_plan;
+
+/* ---------------------------------------------------------------- basics */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *bc_last_error(void);
+int bc_abi_version(void);
+int bc_device_count(int *count);
+
+/* One context per GPU: owns a non-blocking stream, a plan cache and a small
+ * device status word used by kernels to report bad inputs.
+ * Replaces WgpuDevice creation (device/wgpu_device/). */
+int bc_ctx_create(int device, bc_ctx **out);
+int bc_ctx_destroy(bc_ctx *ctx);
+int bc_ctx_device(const bc_ctx *ctx, int *device);
+/* cudaStream_t of the context, as void*. */
+int bc_ctx_stream(bc_ctx *ctx, void **stream);
+/* Waits for the context stream, then reports (and clears) any status a
+ * kernel raised since the last check (e.g. a coefficient >= 2^32 given to a
+ * plan whose modulus is below 2^31 -> BC_ERR_INVALID_INPUT). */
+int bc_ctx_sync(bc_ctx *ctx);
+
+/* --------------------------------------------------------------- buffers */
+
+/* Device memory owned by the caller; synchronous copies use the ctx stream. */
+int bc_buf_alloc(bc_ctx *ctx, size_t bytes, void **dptr);
+int bc_buf_free(bc_ctx *ctx, void *dptr);
+int bc_buf_h2d(bc_ctx *ctx, void *dst, const void *src, size_t bytes);
+int bc_buf_d2h(bc_ctx *ctx, void *dst, const void *src, size_t bytes);
+int bc_buf_h2d_async(bc_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream);
+int bc_buf_d2h_async(bc_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream);
+/* Page-locked host memory for the async copies above. */
+int bc_host_alloc(size_t bytes, void **hptr);
+int bc_host_free(void *hptr);
+
+/* ------------------------------------------- reference op API (synchronous)
+ * Each pair is <Op>::new validation (the *_check call: same conditions, same
+ * order, same message text as the Rust constructor) and <Op>::execute (runs
+ * on the context stream and returns after the result is complete, as the
+ * reference's submit + poll does).  Lengths are in u32 words, as
+ * Tensor::len() reports them.  Outputs are caller-allocated (N u64). */
+
+/* fhe_ntt/mod.rs:210-242 (same candidate order and fallbacks). */
+uint64_t bc_compute_primitive_root(uint32_t degree, uint64_t modulus);
+/* fhe_intt/mod.rs:202-204 (extended Euclid; 0 if not invertible). */
+uint64_t bc_compute_inverse_root(uint32_t degree, uint64_t modulus, uint64_t root);
+
+/* fhe_ntt/mod.rs:95-140 / compute.rs:29-143.  Cyclic DIT transform with the
+ * N-th root omega, natural-order output, X_k = sum_j x_j omega^{jk}. */
+int bc_fhe_ntt_check(size_t input_len_u32, uint32_t degree, uint64_t modulus,
+                     uint64_t root_of_unity);
+int bc_fhe_ntt(bc_ctx *ctx, const uint64_t *d_in, size_t input_len_u32, uint32_t degree,
+               uint64_t modulus, uint64_t root_of_unity, uint64_t *d_out);
+
+/* fhe_intt/mod.rs:82-124 / compute.rs:27-168.  DIT with the given inverse
+ * root, then multiplication by N^-1 (0 when N is not invertible mod q). */
+int bc_fhe_intt_check(size_t input_len_u32, uint32_t degree, uint64_t modulus,
+                      uint64_t inv_root_of_unity);
+int bc_fhe_intt(bc_ctx *ctx, const uint64_t *d_in, size_t input_len_u32, uint32_t degree,
+                uint64_t modulus, uint64_t inv_root_of_unity, uint64_t *d_out);
+
+/* fhe_pointwise_mul.rs:64-155.  C[i] = A[i] * B[i] mod q. */
+int bc_fhe_pointwise_mul_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree,
+                               uint64_t modulus);
+int bc_fhe_pointwise_mul(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32,
+                         const uint64_t *d_b, size_t b_len_u32, uint32_t degree,
+                         uint64_t modulus, uint64_t *d_out);
+
+/* fhe_fast_poly_mul.rs:61-154.  INTT(NTT(a) * NTT(b)), fused in one kernel. */
+int bc_fhe_fast_poly_mul_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree,
+                               uint64_t modulus, uint64_t root_of_unity);
+int bc_fhe_fast_poly_mul(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32,
+                         const uint64_t *d_b, size_t b_len_u32, uint32_t degree,
+                         uint64_t modulus, uint64_t root_of_unity, uint64_t *d_out);
+
+/* ------------------------------------------------ batched plans (new path)
+ * A plan holds, for n_limbs RNS limbs of one degree N, the device twiddle
+ * tables (with Shoup companions), N^-1 and the kernel choice.
+ *
+ * BC_NTT_CYCLIC: roots[i] is the N-th root omega_i and inv_roots[i] the root
+ *   used by the inverse (NULL: the modular inverse of roots[i]).  Forward and
+ *   inverse compute exactly the reference's DIT network, for any root value.
+ * BC_NTT_NEGACYCLIC: roots[i] is a primitive 2N-th root psi_i (psi^N == -1
+ *   mod q is checked); forward A_k = sum_j a_j psi^{j(2k+1)}, inverse its
+ *   exact inverse, both in natural order.  inv_roots must be NULL.
+ *
+ * Moduli: q < 2^31 runs 32-bit Shoup arithmetic, 2^31 <= q < 2^62 runs
+ * 64-bit Shoup/Harvey arithmetic; larger moduli are rejected. */
+typedef enum bc_ntt_mode { BC_NTT_CYCLIC = 0, BC_NTT_NEGACYCLIC = 1 } bc_ntt_mode;
+
+/* Element (limb l, polynomial p, coefficient j) of a batch lives at
+ * base[l * limb_stride + p * poly_stride + j] (strides in u64 elements).
+ * A NULL layout means limb-major contiguous: poly_stride = N,
+ * limb_stride = batch * N. */
+typedef struct bc_layout {
+    int64_t limb_stride;
+    int64_t poly_stride;
+} bc_layout;
+
+typedef struct bc_plan_info {
+    uint32_t degree;
+    uint32_t n_limbs;
+    int32_t mode;
+    int32_t word_bits;        /* 32 or 64: arithmetic width chosen from the moduli */
+    int32_t kernel_kind;      /* 0 single-CTA shared memory, 1 cluster, 2 multi-pass */
+    int32_t cluster_size;     /* CTAs per polynomial for kind 1 */
+    uint64_t table_bytes;     /* device bytes of twiddle tables */
+} bc_plan_info;
+
+int bc_plan_create(bc_ctx *ctx, uint32_t degree, uint32_t n_limbs, const uint64_t *moduli,
+                   const uint64_t *roots, const uint64_t *inv_roots, int mode,
+                   bc_plan **out);
+int bc_plan_destroy(bc_plan *plan);
+int bc_plan_info_get(const bc_plan *plan, bc_plan_info *out);
+
+/* Forward / inverse transform of `batch` polynomials per limb (all limbs).
+ * In place (d_in == d_out) is allowed.  Asynchronous on `stream`
+ * (NULL: the context stream). */
+int bc_ntt_forward(bc_plan *plan, const uint64_t *d_in, uint64_t *d_out, uint32_t batch,
+                   const bc_layout *layout, void *stream);
+int bc_ntt_inverse(bc_plan *plan, const uint64_t *d_in, uint64_t *d_out, uint32_t batch,
+                   const bc_layout *layout, void *stream);
+/* C = A * B mod q_l, coefficient-wise. */
+int bc_pointwise_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
+                     uint32_t batch, const bc_layout *layout, void *stream);
+/* C = INTT(NTT(A) * NTT(B)) per (limb, polynomial), one fused kernel. */
+int bc_polymul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
+               uint32_t batch, const bc_layout *layout, void *stream);
+
+/* Seeded synthetic coefficients, uniform in [0, q_l): element (l, p, j) of
+ * the batch gets value(seed, ((l * total_polys + first_poly + p) * N + j)),
+ * value(s, g) = floor(splitmix64(s + (g + 1) * 0x9E3779B97F4A7C15) * q / 2^64). */
+int bc_fill_uniform(bc_plan *plan, uint64_t *d_out, uint32_t batch, const bc_layout *layout,
+                    uint64_t seed, uint64_t first_poly, uint64_t total_polys, void *stream);
+/* Order-sensitive 64-bit digest of `count` u64 words (for cross-GPU checks):
+ * sum_i splitmix64(x_i ^ (i * 0xD1B54A32D192ED03)) mod 2^64, written to *d_out. */
+int bc_digest(bc_ctx *ctx, const uint64_t *d_in, size_t count, uint64_t *d_out, void *stream);
+
+/* ------------------------------------------------------- multi-GPU split */
+/* Contiguous balanced split of `units` over `shards`: shard s gets
+ * [begin, begin + count) with sizes differing by at most one. */
+int bc_partition(uint64_t units, uint32_t shards, uint32_t shard, uint64_t *begin,
+                 uint64_t *count);
+
+/* ------------------------------------------- host helpers (no GPU needed) */
+/* i-th (0-based) largest prime q < 2^bits with q == 1 mod 2N (0 if none). */
+uint64_t bc_ntt_prime(uint32_t bits, uint32_t degree, uint32_t index);
+/* psi = g^((q-1)/2N), g the smallest generator of Z_q^* (q prime). */
+uint64_t bc_negacyclic_root(uint64_t modulus, uint32_t degree);
+/* Host copy of the device twiddle table entry k (1 <= k < N) of limb 0 of a
+ * plan description, without a GPU: table 0 forward, 1 inverse.  Writes the
+ * twiddle and its Shoup companion.  For tests of the table generator. */
+int bc_debug_twiddle(uint32_t degree, uint64_t modulus, uint64_t root, uint64_t inv_root,
+                     int mode, int table, uint32_t k, uint64_t *w, uint64_t *w_shoup);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BARRACUDA_FHE_H */

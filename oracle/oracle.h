@@ -1,0 +1,127 @@
+/*
+ * oracle.h -- CPU restatement of barraCuda's FHE NTT path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the product library links, loads or
+ * calls this code.  It is used by tests/, by __graft_entry__.smoke() and by
+ * the cpu_baseline / --impl reference legs of bench.py, always as the
+ * checker or the timed CPU baseline, never as a path that produces product
+ * output.
+ *
+ * Three parts:
+ *   1. ref_wgsl.c  -- a restatement of the reference's own algorithm: the
+ *      WGSL shaders (u32-pair u64 emulation, low-64-bit multiply, bit-serial
+ *      reduction, bit-reverse + log2 N radix-2 DIT passes with ping-pong
+ *      buffers, separate N^-1 scale pass, pointwise mul with its 32-bit fast
+ *      path and 64-bit Barrett path) and the host-side Rust around them
+ *      (twiddle generation, root search, extended Euclid).  Bit-exact target
+ *      for parity.  Citations are to crates/barracuda/src/ops/... of
+ *      ecoPrimals/barraCuda.
+ *   2. exact.c     -- exact u128 arithmetic: cyclic / negacyclic NTT and
+ *      INTT, schoolbook convolutions, prime search, generators.
+ *   3. baseline.c  -- a threaded driver of part 1 used as the CPU baseline.
+ */
+#ifndef BC_ORACLE_H
+#define BC_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------- part 1: reference restatement ---------------- */
+
+/* fhe_ntt.wgsl:45-70 u64_mul (low 64 bits via 16-bit partial products). */
+uint64_t orc_wgsl_u64_mul(uint64_t a, uint64_t b);
+/* fhe_ntt.wgsl:84-110 u64_mod_simple (bit-serial for m < 2^32, else <=128 subtractions). */
+uint64_t orc_wgsl_u64_mod_simple(uint64_t a, uint64_t m);
+/* fhe_pointwise_mul.wgsl:43-64 mul32_wide -> 64-bit product. */
+uint64_t orc_wgsl_mul32_wide(uint32_t a, uint32_t b);
+/* fhe_pointwise_mul.wgsl:87-141 mod_mul (fast path + 64-bit Barrett path). */
+uint64_t orc_wgsl_pointwise_mod_mul(uint64_t a, uint64_t b, uint64_t q, uint64_t mu);
+
+/* fhe_ntt/mod.rs:174-184 compute_twiddle_factors: out[k] = root^k, k < degree. */
+void orc_ref_twiddles(uint32_t degree, uint64_t modulus, uint64_t root, uint64_t *out);
+/* fhe_ntt/mod.rs:190-204 mod_pow. */
+uint64_t orc_ref_mod_pow(uint64_t base, uint64_t exp, uint64_t modulus);
+/* fhe_ntt/mod.rs:210-242 compute_primitive_root. */
+uint64_t orc_ref_compute_primitive_root(uint32_t degree, uint64_t modulus);
+/* fhe_intt/mod.rs:177-198 compute_modular_inverse (0 when not invertible). */
+uint64_t orc_ref_modinv(uint64_t a, uint64_t m);
+/* fhe_intt/mod.rs:202-204 compute_inverse_root. */
+uint64_t orc_ref_compute_inverse_root(uint32_t degree, uint64_t modulus, uint64_t root);
+/* fhe_fast_poly_mul.rs:176-197 private extended Euclid (no invertibility check). */
+uint64_t orc_ref_fastmul_modinv(uint64_t a, uint64_t m);
+
+/* fhe_ntt/compute.rs:29-143 + fhe_ntt.wgsl: FheNtt::execute on one polynomial.
+ * degree must be a power of two >= 1; no validation here (the op API does it). */
+void orc_ref_ntt(const uint64_t *in, uint64_t *out, uint32_t degree, uint64_t modulus,
+                 uint64_t root);
+/* fhe_intt/compute.rs:27-168 + fhe_intt.wgsl: FheIntt::execute (DIT with the
+ * given inverse root, then the scale_by_n pass with N^-1 from orc_ref_modinv). */
+void orc_ref_intt(const uint64_t *in, uint64_t *out, uint32_t degree, uint64_t modulus,
+                  uint64_t inv_root);
+/* fhe_pointwise_mul.rs:119-155 + .wgsl main: C[i] = A[i]*B[i] mod q. */
+void orc_ref_pointwise(const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t degree,
+                       uint64_t modulus);
+/* fhe_fast_poly_mul.rs:122-154: NTT(a), NTT(b), pointwise, INTT(inv root). */
+void orc_ref_fast_poly_mul(const uint64_t *a, const uint64_t *b, uint64_t *c,
+                           uint32_t degree, uint64_t modulus, uint64_t root);
+
+/* Negacyclic transforms expressed with the reference's own ops:
+ *   forward = FheNtt(omega = psi^2) applied to FhePointwiseMul(a, [psi^j])
+ *   inverse = FhePointwiseMul(FheIntt(A, psi^-2), [psi^-j])            */
+void orc_ref_negacyclic_ntt(const uint64_t *in, uint64_t *out, uint32_t degree,
+                            uint64_t modulus, uint64_t psi);
+void orc_ref_negacyclic_intt(const uint64_t *in, uint64_t *out, uint32_t degree,
+                             uint64_t modulus, uint64_t psi);
+
+/* ---------------- part 2: exact arithmetic ---------------- */
+
+uint64_t orc_mulmod(uint64_t a, uint64_t b, uint64_t q);
+uint64_t orc_powmod(uint64_t a, uint64_t e, uint64_t q);
+int orc_is_prime(uint64_t n);
+/* i-th (0-based) largest prime q < 2^bits with q == 1 mod 2N; 0 if none found. */
+uint64_t orc_ntt_prime(uint32_t bits, uint32_t degree, uint32_t index);
+/* smallest generator of Z_q^* (q prime). */
+uint64_t orc_smallest_generator(uint64_t q);
+/* psi = g^((q-1)/2N) with g the smallest generator. */
+uint64_t orc_psi(uint64_t q, uint32_t degree);
+
+/* exact cyclic transform X_k = sum_j x_j w^{jk} (any w, O(N^2), small N). */
+void orc_exact_dft(const uint64_t *in, uint64_t *out, uint32_t n, uint64_t q, uint64_t w);
+/* exact cyclic NTT in natural order, O(N log N); w must have w^N = 1. Inputs reduced mod q. */
+void orc_exact_ntt(const uint64_t *in, uint64_t *out, uint32_t n, uint64_t q, uint64_t w);
+/* exact negacyclic forward A_k = sum_j a_j psi^{j(2k+1)} (natural order). */
+void orc_exact_negacyclic_ntt(const uint64_t *in, uint64_t *out, uint32_t n, uint64_t q,
+                              uint64_t psi);
+/* exact negacyclic inverse, a_j = N^-1 psi^-j sum_k A_k psi^{-2jk}. */
+void orc_exact_negacyclic_intt(const uint64_t *in, uint64_t *out, uint32_t n, uint64_t q,
+                               uint64_t psi);
+/* schoolbook products mod (X^N - 1) and mod (X^N + 1). */
+void orc_cyclic_convolution(const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t n,
+                            uint64_t q);
+void orc_negacyclic_convolution(const uint64_t *a, const uint64_t *b, uint64_t *c,
+                                uint32_t n, uint64_t q);
+
+/* Counter-based input generator shared with the product's device generator:
+ * value(seed, g) = floor(splitmix64(seed + (g+1)*0x9E3779B97F4A7C15) * q / 2^64). */
+uint64_t orc_seeded_value(uint64_t seed, uint64_t g, uint64_t q);
+void orc_seeded_fill(uint64_t *out, size_t count, uint64_t seed, uint64_t g0, uint64_t q);
+
+/* ---------------- part 3: threaded CPU baseline ---------------- */
+
+/* Runs orc_ref_ntt (kind 0), orc_ref_intt (kind 1), orc_ref_negacyclic_ntt (2),
+ * orc_ref_negacyclic_intt (3) or an exact O(N log N) negacyclic forward (4) on
+ * `count` polynomials of `degree` coefficients stored back to back, using up
+ * to `threads` POSIX threads.  Polynomial p uses modulus moduli[p % n_moduli]
+ * and root roots[p % n_moduli].  Returns the wall time in seconds. */
+double orc_baseline_run(int kind, const uint64_t *in, uint64_t *out, uint32_t degree,
+                        uint32_t count, const uint64_t *moduli, const uint64_t *roots,
+                        uint32_t n_moduli, int threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,190 @@
+"""Pins the CPU oracle (oracle/, a C restatement of the reference WGSL path)
+against the reference's own known answers and against exact arithmetic."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.helpers import compute_primitive_root, find_root_of_unity, modinv, random_poly, resolve_root
+
+L = O.lib()
+
+
+def test_golden_cases(kats):
+    rng = np.random.default_rng(7)
+    for c in kats["cases"]:
+        k = c["kind"]
+        if k == "twiddles":
+            assert list(O.ref_twiddles(c["degree"], c["modulus"], c["root"])) == c["expect"], c["name"]
+        elif k == "modinv":
+            assert L.orc_ref_modinv(c["a"], c["m"]) == c["expect"], c["name"]
+        elif k == "inverse_root":
+            assert L.orc_ref_compute_inverse_root(c["degree"], c["modulus"], c["root"]) == c["expect"]
+        elif k == "ntt":
+            assert list(O.ref_ntt(c["input"], c["degree"], c["modulus"], c["root"])) == c["expect"]
+        elif k == "roundtrip":
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            back = O.ref_intt(O.ref_ntt(c["input"], n, q, r), n, q, modinv(r, q))
+            assert [int(v) % q for v in back] == [v % q for v in c["input"]], c["name"]
+        elif k == "linearity":
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            a, b = np.array(c["a"], np.uint64), np.array(c["b"], np.uint64)
+            lhs = O.ref_ntt((a + b) % np.uint64(q), n, q, r)
+            rhs = (O.ref_ntt(a, n, q, r) + O.ref_ntt(b, n, q, r)) % np.uint64(q)
+            assert (lhs == rhs).all()
+        elif k == "ntt_zero":
+            n, q = c["degree"], c["modulus"]
+            assert (O.ref_ntt(c["input"], n, q, resolve_root(c["root"], n, q)) == 0).all()
+        elif k == "ntt_range":
+            n, q = c["degree"], c["modulus"]
+            assert (O.ref_ntt(c["input"], n, q, resolve_root(c["root"], n, q)) < q).all()
+        elif k == "pointwise":
+            assert list(O.ref_pointwise(c["a"], c["b"], c["degree"], c["modulus"])) == c["expect"]
+        elif k == "pointwise_identity":
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            x = random_poly(rng, n, q)
+            one = np.zeros(n, np.uint64)
+            one[0] = 1
+            got = O.ref_pointwise(O.ref_ntt(x, n, q, r), O.ref_ntt(one, n, q, r), n, q)
+            assert (got == O.ref_ntt(x, n, q, r)).all()
+        elif k == "pointwise_zero":
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            x = random_poly(rng, n, q)
+            got = O.ref_pointwise(O.ref_ntt(x, n, q, r), O.ref_ntt(np.zeros(n, np.uint64), n, q, r), n, q)
+            assert (got == 0).all()
+        elif k == "fast_mul_naive":
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            a, b = random_poly(rng, n, q), random_poly(rng, n, q)
+            assert (O.ref_fast_poly_mul(a, b, n, q, r) == O.cyclic_convolution(a, b, n, q)).all()
+        elif k == "fast_mul_commutative":
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            a, b = random_poly(rng, n, q), random_poly(rng, n, q)
+            assert (O.ref_fast_poly_mul(a, b, n, q, r) == O.ref_fast_poly_mul(b, a, n, q, r)).all()
+        elif k == "fast_mul_distributive":
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            a, b, cc = (random_poly(rng, n, q) for _ in range(3))
+            lhs = O.ref_fast_poly_mul(a, (b + cc) % np.uint64(q), n, q, r)
+            rhs = (O.ref_fast_poly_mul(a, b, n, q, r) + O.ref_fast_poly_mul(a, cc, n, q, r)) % np.uint64(q)
+            assert (lhs == rhs).all()
+        else:
+            raise AssertionError(f"unknown kind {k}")
+
+
+def test_known_roots_and_ntt_params(kats):
+    for d, m, r in kats["known_roots"]["values"]:
+        assert pow(r, d, m) == 1 and pow(r, d // 2, m) != 1
+        assert find_root_of_unity(d, m) == r
+    for m, d in kats["ntt_params"]["values"]:
+        r = compute_primitive_root(d, m)
+        assert pow(r, d, m) == 1 and pow(r, d // 2, m) != 1, (m, d, r)
+
+
+def test_wgsl_helpers_are_exact_products():
+    rng = np.random.default_rng(1)
+    for _ in range(2000):
+        a, b = (int(x) for x in rng.integers(0, 2**64, 2, dtype=np.uint64))
+        assert L.orc_wgsl_u64_mul(a, b) == (a * b) % 2**64
+        a32, b32 = a & 0xFFFFFFFF, b & 0xFFFFFFFF
+        assert L.orc_wgsl_mul32_wide(a32, b32) == a32 * b32
+
+
+@pytest.mark.parametrize("n", [2, 4, 8, 64, 256])
+def test_reference_restatement_exact_below_2_31(n):
+    """For q < 2^31 the reference chain is exact: restatement == u128 math."""
+    rng = np.random.default_rng(n)
+    for bits in (14, 20, 30, 31):
+        q = O.ntt_prime(bits, n, 0)
+        psi = O.psi(q, n)
+        w = L.orc_mulmod(psi, psi, q)
+        x = random_poly(rng, n, q)
+        assert (O.ref_ntt(x, n, q, w) == O.exact_ntt(x, n, q, w)).all()
+        assert (O.ref_ntt(x, n, q, w) == O.exact_dft(x, n, q, w)).all()
+        assert (O.ref_negacyclic_ntt(x, n, q, psi) == O.exact_negacyclic_ntt(x, n, q, psi)).all()
+        X = O.exact_negacyclic_ntt(x, n, q, psi)
+        assert (O.ref_negacyclic_intt(X, n, q, psi) == x).all()
+        assert (O.exact_negacyclic_intt(X, n, q, psi) == x).all()
+
+
+def test_reference_diverges_at_or_above_2_31():
+    """Pins (documents) the reference's truncated arithmetic for wide moduli:
+    fhe_ntt.wgsl:45-110 keeps only the low 64 product bits and its bit-serial
+    reduction overflows once q >= 2^31.  The CUDA path computes exact residues
+    there instead, so parity with the reference is claimed only below 2^31."""
+    n = 64
+    rng = np.random.default_rng(3)
+    for bits in (32, 60):
+        q = O.ntt_prime(bits, n, 0)
+        psi = O.psi(q, n)
+        w = L.orc_mulmod(psi, psi, q)
+        x = random_poly(rng, n, q)
+        ref = O.ref_ntt(x, n, q, w)
+        assert not (ref % np.uint64(q) == O.exact_ntt(x, n, q, w)).all()
+
+
+def test_reference_domain_extends_to_u32_inputs():
+    """For q < 2^31 and inputs below 2^32 (not necessarily < q) the reference
+    output, canonically reduced, is the exact transform of x mod q."""
+    rng = np.random.default_rng(11)
+    for n in (4, 16, 128):
+        q = O.ntt_prime(31, n, 0)
+        w = L.orc_mulmod(O.psi(q, n), O.psi(q, n), q)
+        x = rng.integers(0, 2**32, n, dtype=np.uint64)
+        ref = O.ref_ntt(x, n, q, w) % np.uint64(q)
+        assert (ref == O.exact_ntt(x % np.uint64(q), n, q, w)).all()
+        inv = O.ref_intt(x, n, q, modinv(w, q)) % np.uint64(q)
+        back = O.exact_ntt(x % np.uint64(q), n, q, modinv(w, q))
+        ninv = modinv(n, q)
+        assert (inv == np.array([L.orc_mulmod(int(v), ninv, q) for v in back], np.uint64)).all()
+
+
+@pytest.mark.parametrize("n", [4, 8, 32, 256])
+def test_negacyclic_chain_is_negacyclic_convolution(n):
+    rng = np.random.default_rng(n + 100)
+    q = O.ntt_prime(31, n, 2)
+    psi = O.psi(q, n)
+    a, b = random_poly(rng, n, q), random_poly(rng, n, q)
+    A, B = O.ref_negacyclic_ntt(a, n, q, psi), O.ref_negacyclic_ntt(b, n, q, psi)
+    C = O.ref_pointwise(A, B, n, q)
+    assert (O.ref_negacyclic_intt(C, n, q, psi) == O.negacyclic_convolution(a, b, n, q)).all()
+
+
+def test_invalid_root_canary_is_structure_dependent():
+    """validate_gpu.rs:277 passes omega = 11 for N = 8, q = 12289, but
+    11^8 != 1 mod 12289: the forward output is not a DFT, so only the
+    reference's DIT network reproduces it (the round trip still holds)."""
+    n, q, w = 8, 12289, 11
+    assert pow(w, n, q) != 1
+    x = np.arange(1, 9, dtype=np.uint64)
+    assert not (O.ref_ntt(x, n, q, w) == O.exact_dft(x, n, q, w)).all()
+    assert (O.ref_intt(O.ref_ntt(x, n, q, w), n, q, modinv(w, q)) == x).all()
+
+
+def test_prime_families_match_plan():
+    # SURVEY 8(d) examples of the two prime families
+    assert O.ntt_prime(31, 1 << 12, 0) == 2147377153
+    assert O.ntt_prime(31, 1 << 14, 0) == 2147352577
+    assert O.ntt_prime(31, 1 << 16, 0) == 2147352577
+    assert O.ntt_prime(31, 1 << 17, 0) == 2146959361
+    assert O.ntt_prime(60, 1 << 12, 0) == 1152921504606830593
+    assert O.ntt_prime(60, 1 << 14, 0) == 1152921504606748673
+    assert O.ntt_prime(60, 1 << 16, 0) == 1152921504606584833
+    for n in (1 << 12, 1 << 16, 1 << 17):
+        for i in range(3):
+            q = O.ntt_prime(31, n, i)
+            assert L.orc_is_prime(q) and (q - 1) % (2 * n) == 0 and q < 2**31
+            psi = O.psi(q, n)
+            assert L.orc_powmod(psi, n, q) == q - 1
+
+
+def test_seeded_generator_uniform_range():
+    q = O.ntt_prime(31, 4096, 0)
+    v = O.seeded_fill(1 << 16, 0, 0, q)
+    assert (v < q).all()
+    assert abs(float(v.mean()) / q - 0.5) < 0.01
+    assert O.seeded_fill(8, 5, 100, q).tolist() == [L.orc_seeded_value(5, 100 + i, q) for i in range(8)]

@@ -1,0 +1,338 @@
+"""GPU parity of the CUDA path against the CPU oracle and the reference's
+known answers.  Everything runs through the C ABI (libbarracuda_fhe.so).
+
+Bar: bit-exact.  For moduli below 2^31 the target is the reference's own
+algorithm (oracle/ref_wgsl.c); for wider moduli, where the reference
+truncates its products, the target is exact u128 arithmetic."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import barracuda_b200 as bc
+from barracuda_b200 import _native as N
+from oracle import oracle as O
+from tests.helpers import find_root_of_unity, modinv, random_poly, resolve_root
+
+pytestmark = pytest.mark.gpu
+OL = O.lib()
+
+
+def upload(dev, arr):
+    return bc.FheTensor.from_u32(np.ascontiguousarray(np.asarray(arr, np.uint64)).view(np.uint32), dev)
+
+
+def ntt(dev, x, n, q, r):
+    return np.array(bc.FheNtt.new(upload(dev, x), n, q, r).execute().to_u64())
+
+
+def intt(dev, x, n, q, r):
+    return np.array(bc.FheIntt.new(upload(dev, x), n, q, r).execute().to_u64())
+
+
+# ------------------------------------------------------------ reference ops
+
+def test_golden_cases_on_gpu(device, kats):
+    rng = np.random.default_rng(17)
+    for c in kats["cases"]:
+        k, name = c["kind"], c["name"]
+        if k == "ntt":
+            assert list(ntt(device, c["input"], c["degree"], c["modulus"], c["root"])) == c["expect"], name
+        elif k == "roundtrip":
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            back = intt(device, ntt(device, c["input"], n, q, r), n, q, bc.compute_inverse_root(n, q, r))
+            assert [int(v) for v in back] == [v % q for v in c["input"]], name
+        elif k == "linearity":
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            a, b = np.array(c["a"], np.uint64), np.array(c["b"], np.uint64)
+            lhs = ntt(device, (a + b) % np.uint64(q), n, q, r)
+            assert (lhs == (ntt(device, a, n, q, r) + ntt(device, b, n, q, r)) % np.uint64(q)).all()
+        elif k == "ntt_zero":
+            n, q = c["degree"], c["modulus"]
+            assert (ntt(device, c["input"], n, q, resolve_root(c["root"], n, q)) == 0).all()
+        elif k == "ntt_range":
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            got = ntt(device, c["input"], n, q, r)
+            assert (got < q).all() and (got == O.ref_ntt(c["input"], n, q, r)).all()
+        elif k == "pointwise":
+            n, q = c["degree"], c["modulus"]
+            out = bc.FhePointwiseMul.new(upload(device, c["a"]), upload(device, c["b"]), n, q).execute()
+            assert [int(v) for v in out.to_u64()] == c["expect"]
+        elif k in ("pointwise_identity", "pointwise_zero"):
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            x = random_poly(rng, n, q)
+            other = np.zeros(n, np.uint64)
+            if k == "pointwise_identity":
+                other[0] = 1
+            X = bc.FheNtt.new(upload(device, x), n, q, r).execute()
+            Y = bc.FheNtt.new(upload(device, other), n, q, r).execute()
+            got = bc.FhePointwiseMul.new(X, Y, n, q).execute().to_u64()
+            want = O.ref_ntt(x, n, q, r) if k == "pointwise_identity" else np.zeros(n, np.uint64)
+            assert (got == want).all(), name
+        elif k.startswith("fast_mul"):
+            n, q = c["degree"], c["modulus"]
+            r = resolve_root(c["root"], n, q)
+            a, b, cc = (random_poly(rng, n, q) for _ in range(3))
+
+            def fm(x, y):
+                return bc.FheFastPolyMul.new(upload(device, x), upload(device, y), n, q, r).execute().to_u64()
+            if k == "fast_mul_naive":
+                assert (fm(a, b) == O.cyclic_convolution(a, b, n, q)).all()
+            elif k == "fast_mul_commutative":
+                assert (fm(a, b) == fm(b, a)).all()
+            else:
+                lhs = fm(a, (b + cc) % np.uint64(q))
+                assert (lhs == (fm(a, b) + fm(a, cc)) % np.uint64(q)).all()
+
+
+@pytest.mark.parametrize("logn", list(range(1, 15)))
+def test_fhe_ntt_intt_match_reference_restatement(device, logn):
+    n = 1 << logn
+    rng = np.random.default_rng(logn)
+    for bits in (14, 30, 31):
+        q = O.ntt_prime(bits, n, 1)
+        if q == 0:
+            continue
+        psi = O.psi(q, n)
+        w = OL.orc_mulmod(psi, psi, q)
+        x = random_poly(rng, n, q)
+        got = ntt(device, x, n, q, w)
+        assert (got == O.ref_ntt(x, n, q, w)).all(), (n, q)
+        winv = bc.compute_inverse_root(n, q, w)
+        assert (intt(device, got, n, q, winv) == x).all()
+        assert (intt(device, x, n, q, winv) == O.ref_intt(x, n, q, winv)).all()
+
+
+def test_structure_faithful_for_invalid_roots(device):
+    """Roots that are not primitive N-th roots (the canary's omega = 11 for
+    N = 8, arbitrary values) still reproduce the reference's DIT output."""
+    rng = np.random.default_rng(5)
+    for n, q, w in [(8, 12289, 11), (64, 12289, 3), (1024, 12289, 7), (4096, 2147352577, 12345),
+                    (16, 257, 256), (4, 17, 0), (32, 97, 1)]:
+        x = random_poly(rng, n, q)
+        assert (ntt(device, x, n, q, w) == O.ref_ntt(x, n, q, w)).all(), (n, q, w)
+        assert (intt(device, x, n, q, w) == O.ref_intt(x, n, q, w)).all(), (n, q, w)
+
+
+def test_inputs_below_2_32_match_reference_after_reduction(device):
+    rng = np.random.default_rng(9)
+    for n in (4, 256, 4096):
+        q = O.ntt_prime(31, n, 0)
+        w = OL.orc_mulmod(O.psi(q, n), O.psi(q, n), q)
+        x = rng.integers(0, 2**32, n, dtype=np.uint64)
+        assert (ntt(device, x, n, q, w) == O.ref_ntt(x, n, q, w) % np.uint64(q)).all()
+
+
+def test_wide_input_reports_invalid_input_and_device_survives(device):
+    n, q = 16, 12289
+    w = find_root_of_unity(n, q)
+    x = np.ones(n, np.uint64)
+    x[3] = 1 << 40
+    with pytest.raises(bc.BarracudaError) as e:
+        ntt(device, x, n, q, w)
+    assert e.value.kind == "InvalidInput"
+    # the context is still usable afterwards (fhe_fault_tests.rs:95-128)
+    y = random_poly(np.random.default_rng(0), n, q)
+    assert (ntt(device, y, n, q, w) == O.ref_ntt(y, n, q, w)).all()
+
+
+def test_intt_edge_cases(device):
+    # degree 1 (allowed by FheIntt::new), non-congruent and even moduli
+    for n, q, r in [(1, 17, 1), (1, 2**31 - 1, 5), (8, 100, 3), (16, 19, 2), (4, 2, 1), (8, 1, 0)]:
+        x = np.arange(n, dtype=np.uint64) % np.uint64(q)
+        assert (intt(device, x, n, q, r) == O.ref_intt(x, n, q, r) % np.uint64(q)).all(), (n, q)
+
+
+def test_modulus_one(device):
+    # q = 1 passes FheNtt's congruence check; every residue is 0
+    for n in (2, 16):
+        assert (ntt(device, np.zeros(n, np.uint64), n, 1, 0) == 0).all()
+
+
+def test_pointwise_matches_reference(device):
+    rng = np.random.default_rng(2)
+    for n, q in [(4, 12289), (1024, 2147352577), (65536, 998244353), (8, 3)]:
+        a = rng.integers(0, 2**32, n, dtype=np.uint64)
+        b = rng.integers(0, 2**32, n, dtype=np.uint64)
+        got = bc.FhePointwiseMul.new(upload(device, a), upload(device, b), n, q).execute().to_u64()
+        assert (got == O.ref_pointwise(a, b, n, q)).all(), (n, q)
+    # modulus 0: the reference keeps the low 32 bits of each product
+    a = rng.integers(0, 2**32, 16, dtype=np.uint64)
+    b = rng.integers(0, 2**32, 16, dtype=np.uint64)
+    got = bc.FhePointwiseMul.new(upload(device, a), upload(device, b), 16, 0).execute().to_u64()
+    assert (got == O.ref_pointwise(a, b, 16, 0)).all()
+
+
+@pytest.mark.parametrize("logn", [2, 5, 10, 12, 14, 15, 16])
+def test_fast_poly_mul_matches_reference_chain(device, logn):
+    n = 1 << logn
+    rng = np.random.default_rng(logn + 50)
+    q = O.ntt_prime(31, n, 0)
+    w = OL.orc_mulmod(O.psi(q, n), O.psi(q, n), q)
+    a, b = random_poly(rng, n, q), random_poly(rng, n, q)
+    got = bc.FheFastPolyMul.new(upload(device, a), upload(device, b), n, q, w).execute().to_u64()
+    assert (got == O.ref_fast_poly_mul(a, b, n, q, w)).all()
+    if n <= 1024:
+        assert (got == O.cyclic_convolution(a, b, n, q)).all()
+
+
+def test_wide_moduli_are_exact(device):
+    """Moduli in [2^31, 2^62): exact residues (the reference diverges here)."""
+    rng = np.random.default_rng(8)
+    for bits in (32, 45, 60, 62):
+        for n in (4, 64, 4096):
+            q = O.ntt_prime(bits, n, 0)
+            w = OL.orc_mulmod(O.psi(q, n), O.psi(q, n), q)
+            x = random_poly(rng, n, q)
+            got = ntt(device, x, n, q, w)
+            assert (got == O.exact_ntt(x, n, q, w)).all(), (bits, n)
+            assert (intt(device, got, n, q, bc.compute_inverse_root(n, q, w)) == x).all()
+
+
+# ------------------------------------------------------------ batched plans
+
+def _plan(device, n, limbs, bits, mode):
+    qs = bc.ntt_primes(bits, n, limbs)
+    roots = [bc.negacyclic_root(q, n) for q in qs]
+    if mode == bc.CYCLIC:
+        roots = [r * r % q for r, q in zip(roots, qs)]
+    return bc.NttPlan(device, n, qs, roots, mode=mode), qs, roots
+
+
+def _alloc(device, count):
+    return bc.FheTensor(device, 2 * count)
+
+
+@pytest.mark.parametrize("logn,limbs,batch", [(12, 1, 1), (12, 3, 5), (14, 4, 3), (15, 2, 2),
+                                              (16, 2, 2), (17, 1, 2), (10, 8, 9), (3, 2, 7)])
+@pytest.mark.parametrize("bits", [31, 60])
+def test_plan_negacyclic_matches_oracle(device, logn, limbs, batch, bits):
+    n = 1 << logn
+    plan, qs, psis = _plan(device, n, limbs, bits, bc.NEGACYCLIC)
+    total = limbs * batch * n
+    src, dst, back = _alloc(device, total), _alloc(device, total), _alloc(device, total)
+    plan.fill_uniform(src, batch, seed=1234)
+    plan.forward(src, dst, batch)
+    plan.inverse(dst, back, batch)
+    device.synchronize()
+    x, X, xb = src.to_u64(), dst.to_u64(), back.to_u64()
+    assert (xb == x).all()
+    for l in range(limbs):
+        q = qs[l]
+        assert (x[l * batch * n:(l + 1) * batch * n] < q).all()
+        # seeded generator parity with the oracle
+        assert (x[l * batch * n: l * batch * n + 64] == O.seeded_fill(64, 1234, l * batch * n, q)).all()
+        for p in {0, batch - 1}:
+            off = (l * batch + p) * n
+            want = (O.ref_negacyclic_ntt(x[off:off + n], n, q, psis[l]) if bits == 31
+                    else O.exact_negacyclic_ntt(x[off:off + n], n, q, psis[l]))
+            assert (X[off:off + n] == want).all(), (l, p)
+
+
+@pytest.mark.parametrize("logn,limbs,batch", [(12, 2, 3), (14, 2, 2), (16, 1, 2)])
+def test_plan_cyclic_matches_reference(device, logn, limbs, batch):
+    n = 1 << logn
+    plan, qs, ws = _plan(device, n, limbs, 31, bc.CYCLIC)
+    total = limbs * batch * n
+    src, dst, back = _alloc(device, total), _alloc(device, total), _alloc(device, total)
+    plan.fill_uniform(src, batch, seed=99)
+    plan.forward(src, dst, batch)
+    plan.inverse(dst, back, batch)
+    device.synchronize()
+    x, X = src.to_u64(), dst.to_u64()
+    assert (back.to_u64() == x).all()
+    for l in range(limbs):
+        off = l * batch * n
+        assert (X[off:off + n] == O.ref_ntt(x[off:off + n], n, qs[l], ws[l])).all()
+
+
+def test_plan_strided_ciphertext_layout_and_in_place(device):
+    """[ct][2][limb][N] layout (config 3 shape, reduced) and in-place use."""
+    n, limbs, cts = 1 << 12, 3, 4
+    plan, qs, psis = _plan(device, n, limbs, 31, bc.NEGACYCLIC)
+    lay = bc.Layout(limb_stride=n, poly_stride=limbs * n)
+    total = cts * 2 * limbs * n
+    buf = _alloc(device, total)
+    plan.fill_uniform(buf, 2 * cts, seed=7, layout=lay)
+    x = buf.to_u64().copy()
+    plan.forward(buf, buf, 2 * cts, layout=lay)
+    device.synchronize()
+    X = buf.to_u64()
+    for p in (0, 5):
+        for l in range(limbs):
+            off = p * limbs * n + l * n
+            assert (X[off:off + n] == O.ref_negacyclic_ntt(x[off:off + n], n, qs[l], psis[l])).all()
+    plan.inverse(buf, buf, 2 * cts, layout=lay)
+    device.synchronize()
+    assert (buf.to_u64() == x).all()
+
+
+@pytest.mark.parametrize("logn,bits", [(12, 31), (14, 31), (15, 31), (13, 60)])
+@pytest.mark.parametrize("mode", [bc.NEGACYCLIC, bc.CYCLIC])
+def test_plan_polymul_matches_chain(device, logn, bits, mode):
+    n, limbs, batch = 1 << logn, 2, 2
+    plan, qs, roots = _plan(device, n, limbs, bits, mode)
+    total = limbs * batch * n
+    a, b, c = _alloc(device, total), _alloc(device, total), _alloc(device, total)
+    plan.fill_uniform(a, batch, seed=1)
+    plan.fill_uniform(b, batch, seed=2)
+    plan.polymul(a, b, c, batch)
+    device.synchronize()
+    A, B, C = a.to_u64(), b.to_u64(), c.to_u64()
+    for l in range(limbs):
+        off = (l * batch + 1) * n
+        q, r = qs[l], roots[l]
+        if mode == bc.NEGACYCLIC:
+            if bits == 31:
+                want = O.ref_negacyclic_intt(O.ref_pointwise(O.ref_negacyclic_ntt(A[off:off + n], n, q, r),
+                                                             O.ref_negacyclic_ntt(B[off:off + n], n, q, r), n, q),
+                                             n, q, r)
+            else:
+                Xa = O.exact_negacyclic_ntt(A[off:off + n], n, q, r)
+                Xb = O.exact_negacyclic_ntt(B[off:off + n], n, q, r)
+                want = O.exact_negacyclic_intt(np.array([OL.orc_mulmod(int(u), int(v), q)
+                                                         for u, v in zip(Xa, Xb)], np.uint64), n, q, r)
+        else:
+            if bits == 31:
+                want = O.ref_fast_poly_mul(A[off:off + n], B[off:off + n], n, q, r)
+            else:
+                w = r
+                Xa, Xb = O.exact_ntt(A[off:off + n], n, q, w), O.exact_ntt(B[off:off + n], n, q, w)
+                prod = np.array([OL.orc_mulmod(int(u), int(v), q) for u, v in zip(Xa, Xb)], np.uint64)
+                winv = modinv(w, q)
+                ninv = modinv(n, q)
+                want = np.array([OL.orc_mulmod(int(v), ninv, q) for v in O.exact_ntt(prod, n, q, winv)], np.uint64)
+        assert (C[off:off + n] == want).all(), (l, mode, bits)
+
+
+def test_plan_pointwise(device):
+    n, limbs, batch = 1 << 12, 2, 3
+    plan, qs, _ = _plan(device, n, limbs, 31, bc.NEGACYCLIC)
+    total = limbs * batch * n
+    a, b, c = _alloc(device, total), _alloc(device, total), _alloc(device, total)
+    plan.fill_uniform(a, batch, seed=3)
+    plan.fill_uniform(b, batch, seed=4)
+    plan.pointwise_mul(a, b, c, batch)
+    device.synchronize()
+    A, B, C = a.to_u64(), b.to_u64(), c.to_u64()
+    for l in range(limbs):
+        sl = slice(l * batch * n, (l + 1) * batch * n)
+        assert (C[sl] == O.ref_pointwise(A[sl], B[sl], batch * n, qs[l])).all()
+
+
+def test_digest_is_order_sensitive(device):
+    n = 4096
+    a = np.arange(n, dtype=np.uint64)
+    t = upload(device, a)
+    out = _alloc(device, 1)
+    bc.digest(device, t, n, out)
+    device.synchronize()
+    d1 = int(out.to_u64()[0])
+    t2 = upload(device, a[::-1].copy())
+    bc.digest(device, t2, n, out)
+    device.synchronize()
+    assert d1 != int(out.to_u64()[0])
