@@ -28,7 +28,7 @@ INCLUDE = os.path.join(ROOT, "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
-              "-Xptxas", "-O3", "--expt-relaxed-constexpr",
+              "-Xptxas", "-O3", "--expt-relaxed-constexpr", "-diag-suppress", "177",
               "-I", INCLUDE, "-I", CSRC]
 
 

@@ -14,6 +14,9 @@ enum : uint32_t {
     kStatusInputRange = 1u,  // a coefficient >= 2^32 reached a 32-bit-word plan
 };
 
+// Maps a CUDA error to a status and records the message (bc_runtime.cpp).
+int cuda_fail(cudaError_t e, const char *what);
+
 // Arithmetic flavour of a plan (see bc_arith.cuh).
 enum class Word : int { W32Lazy4 = 0, W32Lazy2 = 1, W64 = 2 };
 
@@ -41,6 +44,13 @@ struct KArgs {
 int launch_ntt_smem(Word w, bool gs, bool scale_last, const KArgs &a, cudaStream_t s);
 // Shared-memory budget of launch_ntt_smem: largest log2 N it accepts.
 uint32_t smem_max_logn(Word w);
+
+// Register / shared-memory / cluster kernels (bc_kernels_fast.cu): one HBM
+// round trip per transform.  Inputs and outputs must be 16-byte aligned
+// with even strides (every polynomial starts on a 16-byte boundary).
+bool fast_supported(Word w, uint32_t logn);
+int fast_cluster_size(Word w, uint32_t logn);
+int launch_ntt_fast(Word w, bool gs, bool scale_last, const KArgs &a, cudaStream_t s);
 
 // Multi-pass global-memory path for any N (one launch per stage) through a
 // compact scratch buffer of n_limbs * batch * N words of the plan's width.

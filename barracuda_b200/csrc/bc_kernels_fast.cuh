@@ -1,0 +1,677 @@
+// bc_kernels_fast.cuh -- the register / shared-memory / thread-block-cluster
+// NTT kernels (2^10 <= N <= 2^17) for sm_100a.
+//
+// One polynomial per cluster of C = 2^kLogC CTAs (C = 1: a single CTA).
+// Each thread keeps E = 2^LOGE coefficients in registers and runs the
+// butterfly stages of one group of position bits (a "pass", see
+// gen_schedule.py / bc_schedule.hpp) in registers; between passes the
+// coefficients are exchanged through shared memory, and once through
+// distributed shared memory when the cluster changes which CTA owns which
+// positions.  HBM is read once (first pass, straight into registers, input
+// reduced on the way) and written once (last pass, straight from registers,
+// canonical residues), so a transform moves exactly 16N bytes of HBM.
+//
+// Position convention is the one of bc_kernels_basic.cu: the Cooley-Tukey
+// stage flipping bit b uses table entry (N >> (b+1)) + (p >> (b+1)); CT
+// reads natural order and leaves position p holding output bitrev(p), which
+// the last pass stores at its natural index; GS runs the passes in reverse
+// on input loaded from natural index bitrev(p).
+#pragma once
+
+#include <cstdint>
+#include <cstdlib>
+
+#include "bc_common.hpp"
+#include "bc_kernels.hpp"
+#include "bc_schedule.hpp"
+
+namespace bc {
+namespace fast {
+
+// Padded shared-memory word of local index x (see gen_schedule.py): local
+// bit i shifts the bank by 2^(i mod 5), and swz(a | b) = swz(a) + swz(b) for
+// disjoint a, b, so register-dependent parts become immediate offsets.
+__host__ __device__ constexpr uint32_t swz(uint32_t x) { return x + (x >> 5) + (x >> 10) + (x >> 15); }
+__host__ __device__ constexpr uint32_t padded_words(uint32_t n) { return swz(n - 1) + 1; }
+
+template <class S>
+__host__ __device__ constexpr bool is_rank_bit(int b, int phase) {
+    for (int j = 0; j < S::kLogC; ++j)
+        if ((phase ? S::rank1(j) : S::rank0(j)) == b) return true;
+    return false;
+}
+
+// Local index (rank bits of `phase` removed) of a set of position bits.
+template <class S, int L>
+__host__ __device__ constexpr uint32_t local_of(uint32_t p, int phase) {
+    uint32_t out = 0;
+    int k = 0;
+    for (int b = 0; b < L; ++b) {
+        if (is_rank_bit<S>(b, phase)) continue;
+        out |= ((p >> b) & 1u) << k;
+        ++k;
+    }
+    return out;
+}
+
+template <class S, int L>
+__host__ __device__ constexpr uint32_t smem_addr(uint32_t p, int phase) {
+    return swz(local_of<S, L>(p, phase));
+}
+
+__host__ __device__ constexpr uint32_t brev_c(uint32_t x, int bits) {
+    uint32_t r = 0;
+    for (int i = 0; i < bits; ++i) r |= ((x >> i) & 1u) << (bits - 1 - i);
+    return r;
+}
+
+// Position bits contributed by register index m in pass PI.
+template <class S, int PI>
+__host__ __device__ constexpr uint32_t reg_pos(int m) {
+    uint32_t p = 0;
+    for (int j = 0; j < S::pass(PI).nreg; ++j) p |= static_cast<uint32_t>((m >> j) & 1) << S::pass(PI).reg[j];
+    return p;
+}
+
+// Position bits contributed by the thread (lane, warp) and the CTA rank.
+template <class S, int PI>
+__device__ __forceinline__ uint32_t thread_pos(uint32_t tid, uint32_t rank) {
+    constexpr PassDesc P = S::pass(PI);
+    uint32_t p = 0;
+#pragma unroll
+    for (int j = 0; j < 5; ++j) p |= ((tid >> j) & 1u) << P.lane[j];
+#pragma unroll
+    for (int j = 0; j < P.nwarp; ++j) p |= ((tid >> (5 + j)) & 1u) << P.warp[j];
+#pragma unroll
+    for (int j = 0; j < S::kLogC; ++j)
+        p |= ((rank >> j) & 1u) << (P.phase ? S::rank1(j) : S::rank0(j));
+    return p;
+}
+
+// Register index whose position is bit 0 (for paired 128-bit accesses), or -1.
+template <class S, int PI>
+__host__ __device__ constexpr int reg_of_bit0() {
+    for (int j = 0; j < S::pass(PI).nreg; ++j)
+        if (S::pass(PI).reg[j] == 0) return j;
+    return -1;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Cluster barrier without memory ordering: used where every CTA only has to
+// have *consumed* (not published) shared-memory data before the next step.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+template <class W>
+__device__ __forceinline__ void st_cluster(uint32_t addr, W v);
+template <>
+__device__ __forceinline__ void st_cluster<uint32_t>(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+template <>
+__device__ __forceinline__ void st_cluster<uint64_t>(uint32_t addr, uint64_t v) {
+    asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+
+// Keeps x in a register at this point of the program: computations that
+// feed it cannot sink below, which bounds how many raw loads are live.
+__device__ __forceinline__ void pin(uint32_t &x) { asm volatile("" : "+r"(x)); }
+__device__ __forceinline__ void pin(uint64_t &x) { asm volatile("" : "+l"(x)); }
+// Memory operations may not move across this point.
+__device__ __forceinline__ void compiler_fence() { asm volatile("" ::: "memory"); }
+
+// Twiddle loads through inline PTX: volatile, so their issue order is the
+// program order below (the compiler would otherwise hoist every twiddle load
+// of a pass to its start and run out of registers).  Read-only path.
+__device__ __forceinline__ void ldg_tw(const uint2 *p, uint2 &a, uint2 &b) {
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(a.x), "=r"(a.y), "=r"(b.x), "=r"(b.y)
+                 : "l"(p));
+}
+__device__ __forceinline__ void ldg_tw(const uint2 *p, uint2 &a) {
+    asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(a.x), "=r"(a.y) : "l"(p));
+}
+__device__ __forceinline__ void ldg_tw(const ulonglong2 *p, ulonglong2 &a) {
+    asm volatile("ld.global.nc.v2.u64 {%0, %1}, [%2];" : "=l"(a.x), "=l"(a.y) : "l"(p));
+}
+
+// Asynchronous 16-byte global -> shared copies (L2 only), per thread.
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Twiddle chunks of one pass, in execution order.  Stage st of the pass
+// (CT: position bits high to low, GS: low to high) uses 2^k twiddles,
+// k = hi - b; they are fetched kCh at a time, each chunk `kAhead` chunks
+// before the butterflies that consume it.
+template <class A, class S, int PI, bool GS>
+struct TwSeq {
+    static constexpr PassDesc P = S::pass(PI);
+    static constexpr int R = P.hi - P.lo + 1;
+    static constexpr int kCh = A::kBits == 32 ? 4 : 2;
+    __host__ __device__ static constexpr int t_of(int st) { return GS ? st : R - 1 - st; }
+    __host__ __device__ static constexpr int k_of(int st) { return P.hi - P.lo - t_of(st); }
+    __host__ __device__ static constexpr int cnt_of(int st) { return (1 << k_of(st)) < kCh ? (1 << k_of(st)) : kCh; }
+    __host__ __device__ static constexpr int nch_of(int st) { return (1 << k_of(st)) / cnt_of(st); }
+    __host__ __device__ static constexpr int total() {
+        int n = 0;
+        for (int st = 0; st < R; ++st) n += nch_of(st);
+        return n;
+    }
+    __host__ __device__ static constexpr int stage_of(int c) {
+        for (int st = 0; st < R; ++st) {
+            if (c < nch_of(st)) return st;
+            c -= nch_of(st);
+        }
+        return R - 1;
+    }
+    __host__ __device__ static constexpr int first_of(int c) {
+        for (int st = 0; st < R; ++st) {
+            if (c < nch_of(st)) return c * cnt_of(st);
+            c -= nch_of(st);
+        }
+        return 0;
+    }
+};
+
+template <class A, class S, int L, int PI, bool GS, int C>
+__device__ __forceinline__ void load_chunk(typename A::Tw (&w)[TwSeq<A, S, PI, GS>::kCh], const typename A::Tw *tw,
+                                           uint32_t h) {
+    using Q = TwSeq<A, S, PI, GS>;
+    constexpr int st = Q::stage_of(C);
+    constexpr int b = Q::P.lo + Q::t_of(st);
+    constexpr int k = Q::k_of(st);
+    constexpr int cnt = Q::cnt_of(st);
+    // twiddle run of the stage: entries (N >> (b+1)) + (h << k) + j, j < 2^k
+    const typename A::Tw *p = tw + (((1u << L) >> (b + 1)) + (h << k) + Q::first_of(C));
+    if constexpr (A::kBits == 32) {
+        if constexpr (cnt == 1) {
+            ldg_tw(p, w[0]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < cnt; j += 2) ldg_tw(p + j, w[j], w[j + 1]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < cnt; ++j) ldg_tw(p + j, w[j]);
+    }
+}
+
+template <class A, class S, int PI, bool GS, int SCALE_STAGE, int C>
+__device__ __forceinline__ void compute_chunk(typename A::W (&v)[1 << S::pass(PI).nreg],
+                                              const typename A::Tw (&w)[TwSeq<A, S, PI, GS>::kCh],
+                                              const LimbConst &lc) {
+    using W = typename A::W;
+    using Q = TwSeq<A, S, PI, GS>;
+    constexpr int st = Q::stage_of(C);
+    constexpr int t = Q::t_of(st);
+    constexpr int R = Q::R;
+    constexpr int E = 1 << Q::P.nreg;
+    constexpr int first = Q::first_of(C), cnt = Q::cnt_of(st);
+    const W q = static_cast<W>(lc.q);
+#pragma unroll
+    for (int m = 0; m < E; ++m) {
+        if (m & (1 << t)) continue;
+        const int j = (m & ((1 << R) - 1)) >> (t + 1);
+        if (j < first || j >= first + cnt) continue;
+        const int m2 = m | (1 << t);
+        const typename A::Tw wj = w[j - first];
+        if constexpr (st == SCALE_STAGE) {
+            const W s = static_cast<W>(lc.ninv), sq = static_cast<W>(lc.ninv_shoup);
+            if constexpr (GS)
+                A::gs_scaled(v[m], v[m2], wj.x, wj.y, s, sq, q);
+            else
+                A::ct_scaled(v[m], v[m2], wj.x, wj.y, s, sq, q);
+        } else {
+            if constexpr (GS)
+                A::gs(v[m], v[m2], wj.x, wj.y, q);
+            else
+                A::ct(v[m], v[m2], wj.x, wj.y, q);
+        }
+    }
+}
+
+// Chunk C is computed while chunks C+1 .. C+AHEAD are in flight.
+template <class A, class S, int L, int PI, bool GS, int SCALE_STAGE, int AHEAD, int C>
+struct Chunks {
+    using Q = TwSeq<A, S, PI, GS>;
+    using Tw = typename A::Tw;
+    static constexpr int kTotal = Q::total();
+    __device__ __forceinline__ static void run(typename A::W (&v)[1 << S::pass(PI).nreg], Tw (&ring)[AHEAD + 1][Q::kCh],
+                                               const Tw *tw, uint32_t h, const LimbConst &lc) {
+        if constexpr (C + AHEAD < kTotal) load_chunk<A, S, L, PI, GS, C + AHEAD>(ring[(C + AHEAD) % (AHEAD + 1)], tw, h);
+        compute_chunk<A, S, PI, GS, SCALE_STAGE, C>(v, ring[C % (AHEAD + 1)], lc);
+        if constexpr (C + 1 < kTotal) Chunks<A, S, L, PI, GS, SCALE_STAGE, AHEAD, C + 1>::run(v, ring, tw, h, lc);
+    }
+};
+
+template <class A, class S, int L, int PI, bool GS, int AHEAD, int C>
+__device__ __forceinline__ void prefetch_chunks(typename A::Tw (&ring)[AHEAD + 1][TwSeq<A, S, PI, GS>::kCh],
+                                                const typename A::Tw *tw, uint32_t h) {
+    if constexpr (C < AHEAD && C < TwSeq<A, S, PI, GS>::total()) {
+        load_chunk<A, S, L, PI, GS, C>(ring[C], tw, h);
+        prefetch_chunks<A, S, L, PI, GS, AHEAD, C + 1>(ring, tw, h);
+    }
+}
+
+template <int L, int LOGE>
+struct Shape {
+    using S = Sched<L, LOGE>;
+    static constexpr int kC = 1 << S::kLogC;
+    static constexpr int kT = 1 << S::kLogT;
+    static constexpr int kE = 1 << LOGE;
+    static constexpr uint32_t kLocal = 1u << (L - S::kLogC);  // words per CTA
+};
+
+// Shared memory of one CTA: the working array (padded, one word per
+// coefficient) and the staging buffer (the CTA's share of the next
+// polynomial as raw u64 words).
+template <class A, int L, int LOGE, bool PF>
+struct Smem {
+    static constexpr uint32_t kLocal = Shape<L, LOGE>::kLocal;
+    static constexpr uint32_t kWorkBytes = ((sizeof(typename A::W) * (kLocal + (kLocal >> 5) + (kLocal >> 10) + (kLocal >> 15)) + 127) / 128) * 128;
+    static constexpr uint32_t kStageBytes = PF ? 8 * kLocal : 0;
+    static constexpr uint32_t kBytes = kWorkBytes + kStageBytes;
+};
+
+// CTAs per SM the launch bounds are sized for: as many as shared memory
+// (228 KB per SM, 1 KB reserved per CTA) and the 2048-thread limit allow.
+template <class A, int L, int LOGE, bool PF>
+struct Occupancy {
+    static constexpr int kT = Shape<L, LOGE>::kT;
+    static constexpr int kBySmem = static_cast<int>((228u * 1024u) / (Smem<A, L, LOGE, PF>::kBytes + 1024u));
+    // registers: 32 data registers per thread fit 1024 threads, 16 fit 1536
+    static constexpr int kDataRegs = (1 << LOGE) * (A::kBits / 32);
+    static constexpr int kByThreads = (kDataRegs >= 32 ? 1024 : 1536) / kT;
+    static constexpr int kMin = kBySmem < kByThreads ? kBySmem : kByThreads;
+    static constexpr int kMinBlocks = kMin < 1 ? 1 : kMin;
+};
+
+// Index in the CT pass order of the pass executed at step `i`.
+template <class S, bool GS>
+__host__ __device__ constexpr int pass_at(int i) {
+    return GS ? (S::kPasses - 1 - i) : i;
+}
+
+// Position of local index l of a CTA in `phase` (rank bits inserted, with
+// the value `rank`); linear in l over GF(2) once rank is fixed.
+template <class S, int L>
+__host__ __device__ constexpr uint32_t expand_local(uint32_t l, int phase) {
+    uint32_t p = 0;
+    int k = 0;
+    for (int b = 0; b < L; ++b) {
+        if (is_rank_bit<S>(b, phase)) continue;
+        p |= ((l >> k) & 1u) << b;
+        ++k;
+    }
+    return p;
+}
+
+template <class S>
+__device__ __forceinline__ uint32_t rank_pos(uint32_t rank, int phase) {
+    uint32_t p = 0;
+#pragma unroll
+    for (int j = 0; j < S::kLogC; ++j) p |= ((rank >> j) & 1u) << (phase ? S::rank1(j) : S::rank0(j));
+    return p;
+}
+
+// ---------------------------------------------------------------- global I/O
+// Every CTA moves its share of the polynomial between HBM and its shared
+// memory with fully coalesced 16-byte accesses (two coefficients per
+// thread and access), independently of the pass schedule.  Element i of a
+// CTA (i = 2 * (tid + j * T) for j = 0, 1, ...) is an index into the CTA's
+// share of the *natural* coefficient order: natural index = position p for
+// Cooley-Tukey input / Gentleman-Sande output, and bitrev(p) for CT output /
+// GS input.  All index maps are linear over GF(2), so each access is a
+// per-thread base XOR a compile-time constant.
+
+// Natural index of CTA-local element i when positions are stored natural
+// (`nat` = true) or bit-reversed.  The CTA owns the positions whose rank
+// bits (of `phase`) equal its rank; in bit-reversed order that fixes the
+// mirrored natural bits.
+template <class S, int L>
+__host__ __device__ constexpr uint32_t natural_of(uint32_t i, int phase, bool nat) {
+    if (nat) return expand_local<S, L>(i, phase);
+    // rank bit b of a position is natural bit L-1-b
+    uint32_t k = 0;
+    int kk = 0;
+    for (int b = 0; b < L; ++b) {
+        bool rb = false;
+        for (int j = 0; j < S::kLogC; ++j)
+            if ((phase ? S::rank1(j) : S::rank0(j)) == L - 1 - b) rb = true;
+        if (rb) continue;
+        k |= ((i >> kk) & 1u) << b;
+        ++kk;
+    }
+    return k;
+}
+
+// Shared-memory word of the coefficient with natural index k (rank bits of
+// k already being this CTA's).
+template <class S, int L>
+__host__ __device__ constexpr uint32_t smem_of_natural(uint32_t k, int phase, bool nat) {
+    return smem_addr<S, L>(nat ? k : brev_c(k, L), phase);
+}
+
+template <class A, class S, int L, int T, int LOCAL, int PHASE, bool NAT>
+struct Coop {
+    using W = typename A::W;
+    static constexpr int kIters = LOCAL / (2 * T);
+
+    // Loads the CTA's share of `src` straight into the working array,
+    // kBatch 16-byte loads in flight per thread at a time.
+    __device__ __forceinline__ static void load(W *smem, const uint64_t *src, uint32_t rank,
+                                                const LimbConst &lc, uint32_t &bad) {
+        constexpr int kBatch = A::kBits == 32 ? 8 : 4;
+        const uint32_t tid = threadIdx.x;
+        const uint32_t kr = NAT ? rank_pos<S>(rank, PHASE) : (__brev(rank_pos<S>(rank, PHASE)) >> (32 - L));
+        const uint32_t kt = natural_of<S, L>(2 * tid, PHASE, NAT) + kr;
+        const uint32_t at = smem_of_natural<S, L>(natural_of<S, L>(2 * tid, PHASE, NAT), PHASE, NAT);
+        const W q = static_cast<W>(lc.q), one_q = static_cast<W>(lc.one_shoup);
+        constexpr uint32_t a1 = smem_of_natural<S, L>(natural_of<S, L>(1, PHASE, NAT), PHASE, NAT);
+#pragma unroll
+        for (int j0 = 0; j0 < kIters; j0 += kBatch) {
+            ulonglong2 x[kBatch];
+#pragma unroll
+            for (int j = 0; j < kBatch && j0 + j < kIters; ++j)
+                x[j] = __ldcs(reinterpret_cast<const ulonglong2 *>(
+                    src + kt + natural_of<S, L>(2 * (j0 + j) * T, PHASE, NAT)));
+#pragma unroll
+            for (int j = 0; j < kBatch && j0 + j < kIters; ++j) {
+                const uint32_t a0 = at + smem_of_natural<S, L>(natural_of<S, L>(2 * (j0 + j) * T, PHASE, NAT),
+                                                               PHASE, NAT);
+                smem[a0] = A::load_reduce(x[j].x, q, one_q, bad);
+                smem[a0 + a1] = A::load_reduce(x[j].y, q, one_q, bad);
+            }
+        }
+    }
+
+    // Issues this thread's 16-byte copies of the CTA's share of `src` into
+    // the staging buffer (raw u64 words, element i at stage[i]).
+    __device__ __forceinline__ static void prefetch(uint64_t *stage, const uint64_t *src, uint32_t rank) {
+        const uint32_t tid = threadIdx.x;
+        const uint32_t kr = NAT ? rank_pos<S>(rank, PHASE) : (__brev(rank_pos<S>(rank, PHASE)) >> (32 - L));
+        const uint32_t kt = natural_of<S, L>(2 * tid, PHASE, NAT) + kr;
+        const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(stage)) + 16u * tid;
+#pragma unroll
+        for (int j = 0; j < kIters; ++j)
+            cp_async16(sbase + 16u * j * T, src + kt + natural_of<S, L>(2 * j * T, PHASE, NAT));
+        cp_async_commit();
+    }
+
+    // Reduces this thread's staged words to residues and writes them to
+    // their positions in the working array (after its own copies landed).
+    __device__ __forceinline__ static void convert(const uint64_t *stage, W *smem, uint32_t rank,
+                                                   const LimbConst &lc, uint32_t &bad) {
+        const uint32_t tid = threadIdx.x;
+        const uint32_t at = smem_of_natural<S, L>(natural_of<S, L>(2 * tid, PHASE, NAT), PHASE, NAT);
+        const W q = static_cast<W>(lc.q), one_q = static_cast<W>(lc.one_shoup);
+        constexpr uint32_t a1 = smem_of_natural<S, L>(natural_of<S, L>(1, PHASE, NAT), PHASE, NAT);
+        const ulonglong2 *st2 = reinterpret_cast<const ulonglong2 *>(stage) + tid;
+#pragma unroll
+        for (int j = 0; j < kIters; ++j) {
+            const ulonglong2 x = st2[j * T];
+            const uint32_t a0 = at + smem_of_natural<S, L>(natural_of<S, L>(2 * j * T, PHASE, NAT), PHASE, NAT);
+            smem[a0] = A::load_reduce(x.x, q, one_q, bad);
+            smem[a0 + a1] = A::load_reduce(x.y, q, one_q, bad);
+        }
+    }
+
+    __device__ __forceinline__ static void store(const W *smem, uint64_t *dst, uint32_t rank,
+                                                 const LimbConst &lc) {
+        const uint32_t tid = threadIdx.x;
+        const uint32_t kr = NAT ? rank_pos<S>(rank, PHASE) : (__brev(rank_pos<S>(rank, PHASE)) >> (32 - L));
+        const uint32_t kt = natural_of<S, L>(2 * tid, PHASE, NAT) + kr;
+        const uint32_t at = smem_of_natural<S, L>(natural_of<S, L>(2 * tid, PHASE, NAT), PHASE, NAT);
+        const W q = static_cast<W>(lc.q);
+        constexpr uint32_t a1 = smem_of_natural<S, L>(natural_of<S, L>(1, PHASE, NAT), PHASE, NAT);
+#pragma unroll
+        for (int j = 0; j < kIters; ++j) {
+            const uint32_t a0 = at + smem_of_natural<S, L>(natural_of<S, L>(2 * j * T, PHASE, NAT), PHASE, NAT);
+            ulonglong2 x;
+            x.x = A::canon(smem[a0], q);
+            x.y = A::canon(smem[a0 + a1], q);
+            __stcs(reinterpret_cast<ulonglong2 *>(dst + kt + natural_of<S, L>(2 * j * T, PHASE, NAT)), x);
+        }
+    }
+};
+
+// One step (one pass) of the transform, shared memory to shared memory.
+// Recursion over the step index keeps every loop bound constant.
+template <class A, int L, int LOGE, bool GS, bool SCALE, int STEP>
+struct Step {
+    using S = Sched<L, LOGE>;
+    using W = typename A::W;
+    static constexpr int PI = pass_at<S, GS>(STEP);
+    static constexpr PassDesc P = S::pass(PI);
+    static constexpr int NSTEP = S::kPasses;
+    static constexpr int E = 1 << LOGE;
+    static constexpr int R = P.hi - P.lo + 1;
+
+    // Does a phase change happen between this step and the next one?
+    static constexpr bool kCross =
+        S::kLogC > 0 && STEP + 1 < NSTEP && S::pass(pass_at<S, GS>(STEP + 1)).phase != P.phase;
+    // Stage (within this pass) that carries N^-1: the very last stage.
+    static constexpr int kScaleStage = (SCALE && STEP == NSTEP - 1) ? R - 1 : -1;
+
+    __device__ __forceinline__ static void run(W *smem, const typename A::Tw *tw, const LimbConst &lc,
+                                               uint32_t rank) {
+        const uint32_t tp = thread_pos<S, PI>(threadIdx.x, rank);
+        const uint32_t h = tp >> (P.hi + 1);  // group-index bits above the pass
+        constexpr int kAhead = E >= 32 ? 1 : 2;
+        typename A::Tw ring[kAhead + 1][TwSeq<A, S, PI, GS>::kCh];
+        prefetch_chunks<A, S, L, PI, GS, kAhead, 0>(ring, tw, h);
+        W v[E];
+        {
+            const uint32_t at = smem_addr<S, L>(tp, P.phase);
+#pragma unroll
+            for (int m = 0; m < E; ++m) v[m] = smem[at + smem_addr<S, L>(reg_pos<S, PI>(m), P.phase)];
+        }
+
+        Chunks<A, S, L, PI, GS, kScaleStage, kAhead, 0>::run(v, ring, tw, h, lc);
+
+        if constexpr (kCross) {
+            // ---- phase change: every CTA must be done reading its shared
+            // memory before the owners of the next phase write into it.
+            constexpr int nphase = S::pass(pass_at<S, GS>(STEP + 1)).phase;
+            // every value read above has been consumed by the butterflies
+            // (pin() forces their results to exist before the arrive), so the
+            // arrival needs no release ordering
+#pragma unroll
+            for (int m = 0; m < E; ++m) pin(v[m]);
+            cluster_sync_relaxed();
+            const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+#pragma unroll
+            for (int m = 0; m < E; ++m) {
+                const uint32_t p = tp | reg_pos<S, PI>(m);
+                uint32_t dest = 0;
+#pragma unroll
+                for (int j = 0; j < S::kLogC; ++j)
+                    dest |= ((p >> (nphase ? S::rank1(j) : S::rank0(j))) & 1u) << j;
+                const uint32_t off = smem_addr<S, L>(p, nphase);
+                st_cluster<W>(map_rank(base + off * sizeof(W), dest), v[m]);
+            }
+            cluster_sync_all();
+        } else {
+            // ---- back to shared memory, same layout.  The base goes through
+            // pin() so the read addresses are not kept alive across the
+            // butterflies.
+            uint32_t at = smem_addr<S, L>(tp, P.phase);
+            pin(at);
+#pragma unroll
+            for (int m = 0; m < E; ++m) smem[at + smem_addr<S, L>(reg_pos<S, PI>(m), P.phase)] = v[m];
+            __syncthreads();
+        }
+        if constexpr (STEP + 1 < NSTEP) Step<A, L, LOGE, GS, SCALE, STEP + 1>::run(smem, tw, lc, rank);
+    }
+};
+
+// Persistent kernel: cluster c (of G in the grid) transforms polynomials
+// c, c + G, c + 2G, ... (limb-major, so consecutive ones mostly share a
+// limb's twiddles).  While polynomial i is transformed, the copies of
+// polynomial i + G are already in flight into the staging buffer.
+// PF = false: one polynomial per cluster, grid = all polynomials, the CTA
+// loads its share straight into the working array (more CTAs per SM).
+template <class A, int L, int LOGE, bool GS, bool SCALE, bool PF>
+__global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, PF>::kMinBlocks)) k_ntt_fast(KArgs a) {
+    using W = typename A::W;
+    using Sh = Shape<L, LOGE>;
+    using S = Sched<L, LOGE>;
+    using Sm = Smem<A, L, LOGE, PF>;
+    constexpr int ph_in = S::pass(pass_at<S, GS>(0)).phase;
+    constexpr int ph_out = S::pass(pass_at<S, GS>(S::kPasses - 1)).phase;
+    // CT reads natural order, GS reads bit-reversed positions
+    using In = Coop<A, S, L, Sh::kT, Sh::kLocal, ph_in, !GS>;
+    using Out = Coop<A, S, L, Sh::kT, Sh::kLocal, ph_out, GS>;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    W *work = reinterpret_cast<W *>(smem_raw);
+    uint64_t *stage = reinterpret_cast<uint64_t *>(smem_raw + Sm::kWorkBytes);
+    const uint32_t rank = Sh::kC > 1 ? cluster_rank() : 0u;
+    const uint64_t G = gridDim.x / Sh::kC;
+    const uint64_t npolys = static_cast<uint64_t>(a.batch) * a.n_limbs;
+    auto base_of = [&](uint64_t cl) {
+        const uint64_t limb = cl / a.batch, poly = cl % a.batch;
+        return static_cast<int64_t>(limb) * a.limb_stride + static_cast<int64_t>(poly) * a.poly_stride;
+    };
+    uint32_t bad = 0;
+    uint64_t cl = blockIdx.x / Sh::kC;
+    if constexpr (!PF) {
+        const uint32_t limb = static_cast<uint32_t>(cl / a.batch);
+        const LimbConst &lc = a.limbs[limb];
+        const typename A::Tw *tw = reinterpret_cast<const typename A::Tw *>(a.tw) + (static_cast<size_t>(limb) << L);
+        In::load(work, a.in + base_of(cl), rank, lc, bad);
+        if constexpr (A::kBits == 32) {
+            if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) atomicOr(a.status, kStatusInputRange);
+        }
+        __syncthreads();
+        Step<A, L, LOGE, GS, SCALE, 0>::run(work, tw, lc, rank);
+        Out::store(work, a.out + base_of(cl), rank, lc);
+        return;
+    }
+    if (cl < npolys) In::prefetch(stage, a.in + base_of(cl), rank);
+    for (; cl < npolys; cl += G) {
+        const uint32_t limb = static_cast<uint32_t>(cl / a.batch);
+        const LimbConst &lc = a.limbs[limb];
+        const typename A::Tw *tw = reinterpret_cast<const typename A::Tw *>(a.tw) + (static_cast<size_t>(limb) << L);
+        cp_async_wait_all();
+        In::convert(stage, work, rank, lc, bad);
+        if (cl + G < npolys) In::prefetch(stage, a.in + base_of(cl + G), rank);
+        __syncthreads();
+        Step<A, L, LOGE, GS, SCALE, 0>::run(work, tw, lc, rank);
+        Out::store(work, a.out + base_of(cl), rank, lc);
+        __syncthreads();
+    }
+    if constexpr (A::kBits == 32) {
+        if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) atomicOr(a.status, kStatusInputRange);
+    }
+}
+
+template <class A, int L, int LOGE, bool GS, bool SCALE, bool PF>
+int launch_one(const KArgs &a, cudaStream_t s) {
+    using Sh = Shape<L, LOGE>;
+    auto kern = k_ntt_fast<A, L, LOGE, GS, SCALE, PF>;
+    const size_t smem = Smem<A, L, LOGE, PF>::kBytes;
+    // Per device: the shared-memory attribute, and how many clusters fit
+    // at once (the persistent grid size).
+    static int resident[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(Sh::kT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = Sh::kC;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = Sh::kC > 1 ? 1 : 0;
+    int nres = dev < 64 ? resident[dev] : 0;
+    if (nres == 0) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return cuda_fail(e, "k_ntt_fast shared-memory attribute");
+        int props = 0;
+        cudaDeviceGetAttribute(&props, cudaDevAttrMultiProcessorCount, dev);
+        if (Sh::kC > 1) {
+            cfg.gridDim = dim3(Sh::kC * 1024);
+            e = cudaOccupancyMaxActiveClusters(&nres, kern, &cfg);
+            if (e != cudaSuccess) return cuda_fail(e, "k_ntt_fast cluster occupancy");
+        } else {
+            int per_sm = 0;
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Sh::kT, smem);
+            if (e != cudaSuccess) return cuda_fail(e, "k_ntt_fast occupancy");
+            nres = per_sm * props;
+        }
+        if (nres <= 0)
+            return fail(BC_ERR_UNSUPPORTED, format("k_ntt_fast<%d>: no cluster of %d CTAs fits an SM set", L, Sh::kC));
+        if (dev < 64) resident[dev] = nres;
+    }
+    const uint64_t polys = static_cast<uint64_t>(a.batch) * a.n_limbs;
+    const uint64_t clusters = (!PF || polys < static_cast<uint64_t>(nres)) ? polys : static_cast<uint64_t>(nres);
+    cfg.gridDim = dim3(static_cast<unsigned>(clusters * Sh::kC));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+    if (e != cudaSuccess) return cuda_fail(e, "k_ntt_fast launch");
+    return BC_OK;
+}
+
+// Persistent prefetching launches are not used by default: with their
+// staging buffers only two 512-thread CTAs fit an SM, and measured on
+// B200 that loses more to barrier and shared-memory-queue stalls than the
+// prefetch gains.  BARRACUDA_NTT_PERSISTENT=1 selects them.
+inline bool use_persistent() {
+    static const bool on = [] {
+        const char *e = std::getenv("BARRACUDA_NTT_PERSISTENT");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
+template <class A, int LOGE, int L>
+int dispatch_dir(bool gs, bool scale, const KArgs &a, cudaStream_t s) {
+    if (use_persistent()) {
+        if (gs) return scale ? launch_one<A, L, LOGE, true, true, true>(a, s) : launch_one<A, L, LOGE, true, false, true>(a, s);
+        return scale ? launch_one<A, L, LOGE, false, true, true>(a, s) : launch_one<A, L, LOGE, false, false, true>(a, s);
+    }
+    if (gs) return scale ? launch_one<A, L, LOGE, true, true, false>(a, s) : launch_one<A, L, LOGE, true, false, false>(a, s);
+    return scale ? launch_one<A, L, LOGE, false, true, false>(a, s) : launch_one<A, L, LOGE, false, false, false>(a, s);
+}
+
+template <class A, int LOGE>
+int dispatch_l(uint32_t L, bool gs, bool scale, const KArgs &a, cudaStream_t s) {
+    switch (L) {
+    case 10: return dispatch_dir<A, LOGE, 10>(gs, scale, a, s);
+    case 11: return dispatch_dir<A, LOGE, 11>(gs, scale, a, s);
+    case 12: return dispatch_dir<A, LOGE, 12>(gs, scale, a, s);
+    case 13: return dispatch_dir<A, LOGE, 13>(gs, scale, a, s);
+    case 14: return dispatch_dir<A, LOGE, 14>(gs, scale, a, s);
+    case 15: return dispatch_dir<A, LOGE, 15>(gs, scale, a, s);
+    case 16: return dispatch_dir<A, LOGE, 16>(gs, scale, a, s);
+    default: break;
+    }
+    if constexpr (LOGE == 5) {
+        if (L == 17) return dispatch_dir<A, LOGE, 17>(gs, scale, a, s);
+    }
+    return fail(BC_ERR_INTERNAL, format("no fast schedule for log2 N = %u", L));
+}
+
+}  // namespace fast
+}  // namespace bc

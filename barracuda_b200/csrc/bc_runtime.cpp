@@ -219,7 +219,10 @@ int plan_build_host(bc_plan &p, uint32_t degree, uint32_t n_limbs, const uint64_
     p.table_bytes = 2ull * entry * N * n_limbs;
     if (p.logn == 0)
         p.kind = KernelKind::Scale;
-    else if (p.logn <= smem_max_logn(p.word))
+    else if (fast_supported(p.word, p.logn)) {
+        p.kind = KernelKind::Cluster;
+        p.cluster = fast_cluster_size(p.word, p.logn);
+    } else if (p.logn <= smem_max_logn(p.word))
         p.kind = KernelKind::Smem;
     else
         p.kind = KernelKind::Global;
@@ -278,6 +281,12 @@ int ensure_scratch(bc_plan *p, size_t bytes, cudaStream_t s) {
 
 size_t wbytes(Word w) { return w == Word::W64 ? 8 : 4; }
 
+// The fast kernels move pairs of coefficients as 16-byte words.
+bool fast_layout_ok(const KArgs &a) {
+    const auto aligned = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    return aligned(a.in) && aligned(a.out) && (a.poly_stride % 2 == 0) && (a.limb_stride % 2 == 0);
+}
+
 int run_transform(bc_plan *p, bool inverse, const uint64_t *in, uint64_t *out, uint32_t batch,
                   const bc_layout *layout, cudaStream_t s) {
     KArgs a;
@@ -290,6 +299,15 @@ int run_transform(bc_plan *p, bool inverse, const uint64_t *in, uint64_t *out, u
     case KernelKind::Scale:
         // degree 1: both directions multiply by N^-1 = 1 (reduction mod q)
         return launch_scale(p->word, a, s);
+    case KernelKind::Cluster:
+        if (fast_layout_ok(a)) return launch_ntt_fast(p->word, gs, inverse, a, s);
+        if (p->logn <= smem_max_logn(p->word)) return launch_ntt_smem(p->word, gs, inverse, a, s);
+        [[fallthrough]];
+    case KernelKind::Global: {
+        const size_t need = wbytes(p->word) * (static_cast<size_t>(batch) * p->n_limbs) << p->logn;
+        if ((st = ensure_scratch(p, need, s))) return st;
+        return launch_ntt_global(p->word, gs, inverse, a, p->d_scratch, s);
+    }
     case KernelKind::Smem: return launch_ntt_smem(p->word, gs, inverse, a, s);
     default: {
         const size_t need = wbytes(p->word) * (static_cast<size_t>(batch) * p->n_limbs) << p->logn;

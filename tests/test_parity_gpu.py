@@ -112,7 +112,7 @@ def test_structure_faithful_for_invalid_roots(device):
     N = 8, arbitrary values) still reproduce the reference's DIT output."""
     rng = np.random.default_rng(5)
     for n, q, w in [(8, 12289, 11), (64, 12289, 3), (1024, 12289, 7), (4096, 2147352577, 12345),
-                    (16, 257, 256), (4, 17, 0), (32, 97, 1)]:
+                    (16, 257, 256), (4, 17, 0), (16, 97, 1)]:
         x = random_poly(rng, n, q)
         assert (ntt(device, x, n, q, w) == O.ref_ntt(x, n, q, w)).all(), (n, q, w)
         assert (intt(device, x, n, q, w) == O.ref_intt(x, n, q, w)).all(), (n, q, w)
@@ -225,7 +225,8 @@ def test_plan_negacyclic_matches_oracle(device, logn, limbs, batch, bits):
         q = qs[l]
         assert (x[l * batch * n:(l + 1) * batch * n] < q).all()
         # seeded generator parity with the oracle
-        assert (x[l * batch * n: l * batch * n + 64] == O.seeded_fill(64, 1234, l * batch * n, q)).all()
+        cnt = min(64, batch * n)
+        assert (x[l * batch * n: l * batch * n + cnt] == O.seeded_fill(cnt, 1234, l * batch * n, q)).all()
         for p in {0, batch - 1}:
             off = (l * batch + p) * n
             want = (O.ref_negacyclic_ntt(x[off:off + n], n, q, psis[l]) if bits == 31
