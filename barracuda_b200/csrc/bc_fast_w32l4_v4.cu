@@ -1,4 +1,4 @@
-// bc_fast_w32l4_e16.cu -- instantiates the fast NTT kernels for 32-bit words, q < 2^30, 16 coefficients per thread.
+// bc_fast_w32l4_v4.cu -- instantiates the fast NTT kernels for 32-bit words, q < 2^30, schedule variant 4.
 #include "bc_kernels_fast.cuh"
 
 namespace bc {

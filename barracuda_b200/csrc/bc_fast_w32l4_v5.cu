@@ -1,4 +1,4 @@
-// bc_fast_w32l4_e32.cu -- instantiates the fast NTT kernels for 32-bit words, q < 2^30, 32 coefficients per thread.
+// bc_fast_w32l4_v5.cu -- instantiates the fast NTT kernels for 32-bit words, q < 2^30, schedule variant 5.
 #include "bc_kernels_fast.cuh"
 
 namespace bc {

@@ -1,4 +1,4 @@
-// bc_fast_w64_e16.cu -- instantiates the fast NTT kernels for 64-bit words, q < 2^62, 16 coefficients per thread.
+// bc_fast_w64_v4.cu -- instantiates the fast NTT kernels for 64-bit words, q < 2^62, schedule variant 4.
 #include "bc_kernels_fast.cuh"
 
 namespace bc {

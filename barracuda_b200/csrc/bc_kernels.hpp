@@ -51,6 +51,12 @@ uint32_t smem_max_logn(Word w);
 bool fast_supported(Word w, uint32_t logn);
 int fast_cluster_size(Word w, uint32_t logn);
 int launch_ntt_fast(Word w, bool gs, bool scale_last, const KArgs &a, cudaStream_t s);
+// Schedule variant the fast kernel uses for a direction, and the position
+// of natural twiddle-table entry knat (= m + i) in that variant's table,
+// which stores each stage's twiddles transposed per pass (pair = 2 for
+// 8-byte entries, 1 for 16-byte entries).
+int fast_variant_for(Word w, uint32_t logn, bool inverse);
+uint64_t fast_table_index(uint32_t L, int V, uint64_t knat, int pair);
 
 // Multi-pass global-memory path for any N (one launch per stage) through a
 // compact scratch buffer of n_limbs * batch * N words of the plan's width.

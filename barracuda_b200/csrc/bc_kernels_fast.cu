@@ -6,6 +6,7 @@
 
 #include "bc_common.hpp"
 #include "bc_kernels.hpp"
+#include "bc_schedule.hpp"
 
 namespace bc {
 namespace fast {
@@ -14,27 +15,48 @@ int dispatch_l(uint32_t L, bool gs, bool scale, const KArgs &a, cudaStream_t s);
 }  // namespace fast
 
 namespace {
-// Coefficients per thread (log2) of the fast kernel for a word size and N:
-// BARRACUDA_NTT_ELEMS=16|32 overrides the default for 32-bit words.
-uint32_t fast_loge(Word w, uint32_t logn) {
-    if (w == Word::W64) return 4;
-    static const int env = [] {
-        const char *e = std::getenv("BARRACUDA_NTT_ELEMS");
-        return e ? std::atoi(e) : 0;
-    }();
-    if (env == 16 && logn <= 16) return 4;
-    if (env == 32) return 5;
-    // 16 coefficients per thread keep two 512-thread CTAs with their
-    // staging buffers resident per SM; N = 2^17 needs 32 (cluster of 8)
-    return logn <= 16 ? 4 : 5;
+// Schedule variant of the fast kernel for a word size and N (see
+// gen_schedule.py): 4 = 16 coefficients per thread in 512-thread CTAs,
+// 5 = 32 per thread in CTAs of up to 2^14 words, 6 = 32 per thread in
+// 256-thread CTAs.  BARRACUDA_NTT_VARIANT=4|5|6 overrides the default for
+// 32-bit words where that schedule exists.
+int env_int(const char *name) {
+    const char *e = std::getenv(name);
+    return e ? std::atoi(e) : 0;
 }
 
-uint32_t sched_logc(uint32_t logn, uint32_t loge) {
-    // local words per CTA: 2^14 for 32 coefficients per thread, 2^13 for 16
-    const uint32_t cap = loge == 5 ? 14 : 13;
-    return logn > cap ? logn - cap : 0;
+int fast_variant(Word w, uint32_t logn, bool inverse) {
+    if (w == Word::W64) return 4;
+    static const int env_all = env_int("BARRACUDA_NTT_VARIANT");
+    static const int env_fwd = env_int("BARRACUDA_NTT_VARIANT_FWD");
+    static const int env_inv = env_int("BARRACUDA_NTT_VARIANT_INV");
+    const int L = static_cast<int>(logn);
+    const int e = inverse ? (env_inv ? env_inv : env_all) : (env_fwd ? env_fwd : env_all);
+    if (e && fast::sched_logc(L, e) >= 0) return e;
+    // Measured on B200 (forward and inverse, ~2 GiB batches): 16 per thread
+    // wins for N <= 2^12, 256-thread CTAs of 32 per thread for 2^14..2^16.
+    if (L <= 12) return 4;
+    if (fast::sched_logc(L, 6) >= 0) return 6;
+    return 5;
 }
 }  // namespace
+
+int fast_variant_for(Word w, uint32_t logn, bool inverse) { return fast_variant(w, logn, inverse); }
+
+uint64_t fast_table_index(uint32_t L, int V, uint64_t knat, int pair) {
+    if (knat == 0) return 0;
+    uint32_t s = 0;
+    while ((knat >> (s + 1)) != 0) ++s;  // m = 2^s butterfly groups
+    const uint64_t m = 1ull << s, i = knat - m;
+    const int b = static_cast<int>(L) - 1 - static_cast<int>(s);
+    const int hi = fast::sched_pass_hi(static_cast<int>(L), V, b);
+    const int k = hi - b;
+    const uint64_t h = i >> k, j = i & ((1ull << k) - 1);
+    const uint64_t H = (1ull << L) >> (hi + 1);
+    if (k == 0) return m + h;
+    const uint64_t P = static_cast<uint64_t>(pair);
+    return m + (j / P) * (P * H) + P * h + (j % P);
+}
 
 bool fast_supported(Word w, uint32_t logn) {
     if (w == Word::W64) return logn >= 10 && logn <= 16;
@@ -43,18 +65,20 @@ bool fast_supported(Word w, uint32_t logn) {
 
 int fast_cluster_size(Word w, uint32_t logn) {
     if (!fast_supported(w, logn)) return 1;
-    return 1 << sched_logc(logn, fast_loge(w, logn));
+    return 1 << fast::sched_logc(static_cast<int>(logn), fast_variant(w, logn, false));
 }
 
 int launch_ntt_fast(Word w, bool gs, bool scale_last, const KArgs &a, cudaStream_t s) {
-    const uint32_t loge = fast_loge(w, a.logn);
+    const int v = fast_variant(w, a.logn, gs || scale_last);
     switch (w) {
     case Word::W32Lazy4:
-        return loge == 4 ? fast::dispatch_l<Arith32<true>, 4>(a.logn, gs, scale_last, a, s)
-                         : fast::dispatch_l<Arith32<true>, 5>(a.logn, gs, scale_last, a, s);
+        if (v == 4) return fast::dispatch_l<Arith32<true>, 4>(a.logn, gs, scale_last, a, s);
+        if (v == 6) return fast::dispatch_l<Arith32<true>, 6>(a.logn, gs, scale_last, a, s);
+        return fast::dispatch_l<Arith32<true>, 5>(a.logn, gs, scale_last, a, s);
     case Word::W32Lazy2:
-        return loge == 4 ? fast::dispatch_l<Arith32<false>, 4>(a.logn, gs, scale_last, a, s)
-                         : fast::dispatch_l<Arith32<false>, 5>(a.logn, gs, scale_last, a, s);
+        if (v == 4) return fast::dispatch_l<Arith32<false>, 4>(a.logn, gs, scale_last, a, s);
+        if (v == 6) return fast::dispatch_l<Arith32<false>, 6>(a.logn, gs, scale_last, a, s);
+        return fast::dispatch_l<Arith32<false>, 5>(a.logn, gs, scale_last, a, s);
     default: return fast::dispatch_l<Arith64, 4>(a.logn, gs, scale_last, a, s);
     }
 }

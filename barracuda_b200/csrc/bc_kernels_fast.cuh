@@ -42,14 +42,15 @@ __host__ __device__ constexpr bool is_rank_bit(int b, int phase) {
 }
 
 // Local index (rank bits of `phase` removed) of a set of position bits.
+// Local index of position bits p in a phase: the schedule's per-phase bit
+// permutation (rank bits dropped), chosen for conflict-free banks.
 template <class S, int L>
 __host__ __device__ constexpr uint32_t local_of(uint32_t p, int phase) {
     uint32_t out = 0;
-    int k = 0;
     for (int b = 0; b < L; ++b) {
-        if (is_rank_bit<S>(b, phase)) continue;
+        const int k = phase ? S::local1(b) : S::local0(b);
+        if (k < 0) continue;
         out |= ((p >> b) & 1u) << k;
-        ++k;
     }
     return out;
 }
@@ -200,18 +201,24 @@ __device__ __forceinline__ void load_chunk(typename A::Tw (&w)[TwSeq<A, S, PI, G
     constexpr int b = Q::P.lo + Q::t_of(st);
     constexpr int k = Q::k_of(st);
     constexpr int cnt = Q::cnt_of(st);
-    // twiddle run of the stage: entries (N >> (b+1)) + (h << k) + j, j < 2^k
-    const typename A::Tw *p = tw + (((1u << L) >> (b + 1)) + (h << k) + Q::first_of(C));
+    // The fast table stores the 2^k twiddles of group h of this stage
+    // transposed, so that the lanes of a warp (different h) read adjacent
+    // words: entry (h, j) at (N >> (b+1)) + (j / P)(P H) + P h + (j % P),
+    // H = N >> (hi+1) groups, P = 2 for 8-byte entries (two per 16-byte
+    // load) and 1 for 16-byte entries.  See fast_table_index().
+    constexpr uint32_t H = (1u << L) >> (Q::P.hi + 1);
+    const typename A::Tw *base = tw + ((1u << L) >> (b + 1));
+    constexpr int j0 = Q::first_of(C);
     if constexpr (A::kBits == 32) {
-        if constexpr (cnt == 1) {
-            ldg_tw(p, w[0]);
+        if constexpr (k == 0) {
+            ldg_tw(base + h, w[0]);
         } else {
 #pragma unroll
-            for (int j = 0; j < cnt; j += 2) ldg_tw(p + j, w[j], w[j + 1]);
+            for (int j = 0; j < cnt; j += 2) ldg_tw(base + (j0 + j) * H + 2 * h, w[j], w[j + 1]);
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < cnt; ++j) ldg_tw(p + j, w[j]);
+        for (int j = 0; j < cnt; ++j) ldg_tw(base + (j0 + j) * H + h, w[j]);
     }
 }
 
@@ -277,7 +284,7 @@ struct Shape {
     using S = Sched<L, LOGE>;
     static constexpr int kC = 1 << S::kLogC;
     static constexpr int kT = 1 << S::kLogT;
-    static constexpr int kE = 1 << LOGE;
+    static constexpr int kE = 1 << S::kLogE;
     static constexpr uint32_t kLocal = 1u << (L - S::kLogC);  // words per CTA
 };
 
@@ -299,7 +306,7 @@ struct Occupancy {
     static constexpr int kT = Shape<L, LOGE>::kT;
     static constexpr int kBySmem = static_cast<int>((228u * 1024u) / (Smem<A, L, LOGE, PF>::kBytes + 1024u));
     // registers: 32 data registers per thread fit 1024 threads, 16 fit 1536
-    static constexpr int kDataRegs = (1 << LOGE) * (A::kBits / 32);
+    static constexpr int kDataRegs = (1 << Sched<L, LOGE>::kLogE) * (A::kBits / 32);
     static constexpr int kByThreads = (kDataRegs >= 32 ? 1024 : 1536) / kT;
     static constexpr int kMin = kBySmem < kByThreads ? kBySmem : kByThreads;
     static constexpr int kMinBlocks = kMin < 1 ? 1 : kMin;
@@ -463,12 +470,17 @@ struct Step {
     static constexpr int PI = pass_at<S, GS>(STEP);
     static constexpr PassDesc P = S::pass(PI);
     static constexpr int NSTEP = S::kPasses;
-    static constexpr int E = 1 << LOGE;
+    static constexpr int E = 1 << S::kLogE;
     static constexpr int R = P.hi - P.lo + 1;
 
     // Does a phase change happen between this step and the next one?
     static constexpr bool kCross =
         S::kLogC > 0 && STEP + 1 < NSTEP && S::pass(pass_at<S, GS>(STEP + 1)).phase != P.phase;
+    // How this step's results reach the next step: CT pass i hands over to
+    // pass i+1 (kind stored on pass i); GS runs them backwards, so step
+    // PI hands over to pass PI-1 (kind stored on pass PI-1).
+    static constexpr int kSync = STEP + 1 >= NSTEP ? kSyncBlock
+                                 : (GS ? S::pass(PI - 1).sync_after : P.sync_after);
     // Stage (within this pass) that carries N^-1: the very last stage.
     static constexpr int kScaleStage = (SCALE && STEP == NSTEP - 1) ? R - 1 : -1;
 
@@ -518,7 +530,11 @@ struct Step {
             pin(at);
 #pragma unroll
             for (int m = 0; m < E; ++m) smem[at + smem_addr<S, L>(reg_pos<S, PI>(m), P.phase)] = v[m];
-            __syncthreads();
+            // warp-local exchange: the next pass reads only what this warp wrote
+            if constexpr (kSync == kSyncWarp)
+                __syncwarp();
+            else
+                __syncthreads();
         }
         if constexpr (STEP + 1 < NSTEP) Step<A, L, LOGE, GS, SCALE, STEP + 1>::run(smem, tw, lc, rank);
     }
@@ -655,20 +671,26 @@ int dispatch_dir(bool gs, bool scale, const KArgs &a, cudaStream_t s) {
     return scale ? launch_one<A, L, LOGE, false, true, false>(a, s) : launch_one<A, L, LOGE, false, false, false>(a, s);
 }
 
-template <class A, int LOGE>
+template <class A, int V, int L>
+int dispatch_if(bool gs, bool scale, const KArgs &a, cudaStream_t s) {
+    if constexpr (sched_logc(L, V) >= 0) return dispatch_dir<A, V, L>(gs, scale, a, s);
+    return fail(BC_ERR_INTERNAL, format("no fast schedule for log2 N = %d, variant %d", L, V));
+}
+
+// Template parameter LOGE of the kernels above is the schedule variant V
+// (Sched<L, V>): 4, 5 or 6, see gen_schedule.py.
+template <class A, int V>
 int dispatch_l(uint32_t L, bool gs, bool scale, const KArgs &a, cudaStream_t s) {
     switch (L) {
-    case 10: return dispatch_dir<A, LOGE, 10>(gs, scale, a, s);
-    case 11: return dispatch_dir<A, LOGE, 11>(gs, scale, a, s);
-    case 12: return dispatch_dir<A, LOGE, 12>(gs, scale, a, s);
-    case 13: return dispatch_dir<A, LOGE, 13>(gs, scale, a, s);
-    case 14: return dispatch_dir<A, LOGE, 14>(gs, scale, a, s);
-    case 15: return dispatch_dir<A, LOGE, 15>(gs, scale, a, s);
-    case 16: return dispatch_dir<A, LOGE, 16>(gs, scale, a, s);
+    case 10: return dispatch_if<A, V, 10>(gs, scale, a, s);
+    case 11: return dispatch_if<A, V, 11>(gs, scale, a, s);
+    case 12: return dispatch_if<A, V, 12>(gs, scale, a, s);
+    case 13: return dispatch_if<A, V, 13>(gs, scale, a, s);
+    case 14: return dispatch_if<A, V, 14>(gs, scale, a, s);
+    case 15: return dispatch_if<A, V, 15>(gs, scale, a, s);
+    case 16: return dispatch_if<A, V, 16>(gs, scale, a, s);
+    case 17: return dispatch_if<A, V, 17>(gs, scale, a, s);
     default: break;
-    }
-    if constexpr (LOGE == 5) {
-        if (L == 17) return dispatch_dir<A, LOGE, 17>(gs, scale, a, s);
     }
     return fail(BC_ERR_INTERNAL, format("no fast schedule for log2 N = %u", L));
 }

@@ -216,7 +216,7 @@ int plan_build_host(bc_plan &p, uint32_t degree, uint32_t n_limbs, const uint64_
             }
         }
     }
-    p.table_bytes = 2ull * entry * N * n_limbs;
+    p.table_bytes = 2ull * entry * N * n_limbs * (fast_supported(p.word, p.logn) ? 2 : 1);
     if (p.logn == 0)
         p.kind = KernelKind::Scale;
     else if (fast_supported(p.word, p.logn)) {
@@ -300,7 +300,10 @@ int run_transform(bc_plan *p, bool inverse, const uint64_t *in, uint64_t *out, u
         // degree 1: both directions multiply by N^-1 = 1 (reduction mod q)
         return launch_scale(p->word, a, s);
     case KernelKind::Cluster:
-        if (fast_layout_ok(a)) return launch_ntt_fast(p->word, gs, inverse, a, s);
+        if (fast_layout_ok(a)) {
+            a.tw = inverse ? p->d_tw_inv_fast : p->d_tw_fwd_fast;
+            return launch_ntt_fast(p->word, gs, inverse, a, s);
+        }
         if (p->logn <= smem_max_logn(p->word)) return launch_ntt_smem(p->word, gs, inverse, a, s);
         [[fallthrough]];
     case KernelKind::Global: {
@@ -562,9 +565,35 @@ int bc_plan_create(bc_ctx *ctx, uint32_t degree, uint32_t n_limbs, const uint64_
         delete p;
         return st;
     }
+    // the fast kernels read each direction's table in their own layout
+    std::vector<unsigned char> fwd_fast, inv_fast;
+    if (p->kind == KernelKind::Cluster) {
+        const size_t entry = p->word == Word::W64 ? 16 : 8;
+        const int pair = p->word == Word::W64 ? 1 : 2;
+        const uint64_t N = degree;
+        for (int t = 0; t < 2; ++t) {
+            const std::vector<unsigned char> &src = t == 0 ? fwd : inv;
+            std::vector<unsigned char> &dst = t == 0 ? fwd_fast : inv_fast;
+            dst.assign(src.size(), 0);
+            const int V = fast_variant_for(p->word, p->logn, t == 1);
+            std::vector<uint64_t> map(N);
+            for (uint64_t k = 1; k < N; ++k) map[k] = fast_table_index(p->logn, V, k, pair);
+            for (uint32_t l = 0; l < n_limbs; ++l) {
+                const unsigned char *sb = src.data() + entry * N * l;
+                unsigned char *db = dst.data() + entry * N * l;
+                for (uint64_t k = 1; k < N; ++k) std::memcpy(db + entry * map[k], sb + entry * k, entry);
+            }
+        }
+    }
     cudaError_t e = cudaMalloc(&p->d_limbs, sizeof(LimbConst) * n_limbs);
     if (e == cudaSuccess) e = cudaMalloc(&p->d_tw_fwd, fwd.size());
     if (e == cudaSuccess) e = cudaMalloc(&p->d_tw_inv, inv.size());
+    if (e == cudaSuccess && !fwd_fast.empty()) e = cudaMalloc(&p->d_tw_fwd_fast, fwd_fast.size());
+    if (e == cudaSuccess && !inv_fast.empty()) e = cudaMalloc(&p->d_tw_inv_fast, inv_fast.size());
+    if (e == cudaSuccess && !fwd_fast.empty())
+        e = cudaMemcpyAsync(p->d_tw_fwd_fast, fwd_fast.data(), fwd_fast.size(), cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess && !inv_fast.empty())
+        e = cudaMemcpyAsync(p->d_tw_inv_fast, inv_fast.data(), inv_fast.size(), cudaMemcpyHostToDevice, ctx->stream);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(p->d_limbs, p->limbs.data(), sizeof(LimbConst) * n_limbs,
                             cudaMemcpyHostToDevice, ctx->stream);
@@ -589,6 +618,8 @@ int bc_plan_destroy(bc_plan *p) {
     cudaFree(p->d_limbs);
     cudaFree(p->d_tw_fwd);
     cudaFree(p->d_tw_inv);
+    cudaFree(p->d_tw_fwd_fast);
+    cudaFree(p->d_tw_inv_fast);
     cudaFree(p->d_scratch);
     delete p;
     return BC_OK;

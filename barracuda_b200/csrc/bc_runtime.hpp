@@ -44,6 +44,8 @@ struct bc_plan {
     bc::LimbConst *d_limbs = nullptr;
     void *d_tw_fwd = nullptr;  // forward CT table
     void *d_tw_inv = nullptr;  // inverse table (CT for cyclic, GS for negacyclic), N^-1 folded
+    void *d_tw_fwd_fast = nullptr;  // the same tables in the fast kernels' layout
+    void *d_tw_inv_fast = nullptr;
     uint64_t table_bytes = 0;
     std::mutex scratch_mu;
     void *d_scratch = nullptr;

@@ -11,19 +11,29 @@ polynomial is spread over the CTAs' shared memories and one exchange (the
 phase change) goes through distributed shared memory.
 
 Per phase the CTA of cluster rank r owns the positions whose `rank` bits
-spell r.  Its shared-memory word of position p is swz(local(p)): local()
-drops the rank bits, swz(x) = x + (x >> 5) + (x >> 10) + (x >> 15) pads the
-array.  Local bit i then moves the bank by 2^(i mod 5), so a warp access is
-free of bank conflicts whenever its 32 lanes vary 5 position bits whose local
-indices are distinct modulo 5; the lane bits of every pass are chosen (and
-checked) that way.  swz is additive over disjoint bits, so every access is a
-per-thread base plus a compile-time offset.
+spell r.  Within a phase, every other position bit has a *local* bit index
+(a per-phase permutation chosen here), and the coefficient of position p
+lives in shared-memory word swz(local(p)) with
+swz(x) = x + (x >> 5) + (x >> 10) + (x >> 15) (one pad word per 32, 1024,
+32768).  Local bit i moves the word by 2^(i mod 5) banks, so a warp access
+is free of bank conflicts when its lanes vary bits whose local indices have
+distinct residues mod 5 (a small search picks the local orders); lanes of
+a pass are listed in residue order.  The guarantee is for 32-bit words: the
+64-bit-word path (moduli >= 2^31) may see 2-way conflicts.  swz is additive
+over disjoint bit sets, so every access is a per-thread base plus a
+compile-time offset.
 
-Lane bits of the first Cooley-Tukey pass are the lowest thread bits
-(coalesced loads of natural-order input); lane bits of the last pass are the
-highest thread bits, highest first, so that consecutive lanes store
-consecutive natural indices bitrev(p).  Gentleman-Sande transforms run the
-same passes in reverse order.
+Lanes and warps: when two consecutive passes of a phase process bit groups
+GA and GB, the first pass puts GB (plus one common bit x) in its lanes and
+the second puts GA (plus x) in its lanes; both keep the same warp bits, so
+the data they exchange never leaves a warp and the pass boundary needs only
+__syncwarp().  Passes that cannot be paired that way exchange through the
+whole CTA (__syncthreads()).
+
+Global memory is read and written by separate cooperative stages (16-byte
+accesses of coefficient pairs in natural order), whose shared-memory
+accesses are constrained the same way.  Gentleman-Sande transforms run the
+passes in reverse order.
 
     python barracuda_b200/csrc/gen_schedule.py   # rewrites bc_schedule.hpp
 """
@@ -35,72 +45,205 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "bc_schedule.hpp")
 
-# (L, loge, logc): (passes [(hi, lo, extras)], rank bits phase 0, rank bits phase 1, split)
+# (L, variant): (loge, logc, passes [(hi, lo, extras)], rank bits phase 0, rank bits phase 1, split)
+# Variants: 4 = 16 coefficients per thread (512-thread CTAs of 2^13 words);
+# 5 = 32 per thread (CTAs of up to 2^14 words); 6 = 32 per thread in
+# 256-thread CTAs of 2^13 words (more, smaller CTAs per SM).
 # `split` = number of passes in phase 0 (the remaining passes are phase 1).
 CONFIGS = {
-    # 32-bit words, 32 coefficients per thread
-    (10, 5, 0): ([(9, 5, []), (4, 0, [])], [], [], 2),
-    (11, 5, 0): ([(10, 10, [0, 1, 2, 3]), (9, 5, []), (4, 0, [])], [], [], 3),
-    (12, 5, 0): ([(11, 10, [0, 1, 2]), (9, 5, []), (4, 0, [])], [], [], 3),
-    (13, 5, 0): ([(12, 10, [0, 1]), (9, 5, []), (4, 0, [])], [], [], 3),
-    (14, 5, 0): ([(13, 10, [0]), (9, 5, []), (4, 0, [])], [], [], 3),
-    (15, 5, 1): ([(14, 10, []), (9, 5, []), (4, 0, [])], [9], [10], 1),
-    (16, 5, 2): ([(15, 13, [0, 1]), (12, 8, []), (7, 5, [0, 1]), (4, 0, [])], [6, 7], [8, 9], 2),
-    (17, 5, 3): ([(16, 13, [0]), (12, 8, []), (7, 5, [0, 1]), (4, 0, [])], [5, 6, 7], [8, 9, 10], 2),
-    # 64-bit words, 16 coefficients per thread
-    (10, 4, 0): ([(9, 8, [0, 1]), (7, 4, []), (3, 0, [])], [], [], 3),
-    (11, 4, 0): ([(10, 8, [0]), (7, 4, []), (3, 0, [])], [], [], 3),
-    (12, 4, 0): ([(11, 8, []), (7, 4, []), (3, 0, [])], [], [], 3),
-    (13, 4, 0): ([(12, 12, [0, 1, 2]), (11, 8, []), (7, 4, []), (3, 0, [])], [], [], 4),
-    (14, 4, 1): ([(13, 12, [0, 1]), (11, 8, []), (7, 4, []), (3, 0, [])], [6], [8], 2),
-    (15, 4, 2): ([(14, 12, [0]), (11, 8, []), (7, 4, []), (3, 0, [])], [5, 6], [8, 9], 2),
-    (16, 4, 3): ([(15, 12, []), (11, 8, []), (7, 4, []), (3, 0, [])], [5, 6, 7], [8, 9, 10], 2),
+    (10, 5): (5, 0, [(9, 5, []), (4, 0, [])], [], [], 2),
+    (11, 5): (5, 0, [(10, 10, [0, 1, 2, 3]), (9, 5, []), (4, 0, [])], [], [], 3),
+    (12, 5): (5, 0, [(11, 10, [0, 1, 2]), (9, 5, []), (4, 0, [])], [], [], 3),
+    (13, 5): (5, 0, [(12, 10, [0, 1]), (9, 5, []), (4, 0, [])], [], [], 3),
+    (14, 5): (5, 0, [(13, 10, [0]), (9, 5, []), (4, 0, [])], [], [], 3),
+    (15, 5): (5, 1, [(14, 10, []), (9, 5, []), (4, 0, [])], [9], [10], 1),
+    (16, 5): (5, 2, [(15, 13, [0, 1]), (12, 8, []), (7, 5, [0, 1]), (4, 0, [])], [6, 7], [8, 9], 2),
+    (17, 5): (5, 3, [(16, 13, [0]), (12, 8, []), (7, 5, [0, 1]), (4, 0, [])], [5, 6, 7], [8, 9, 10], 2),
+    (14, 6): (5, 1, [(13, 10, [0]), (9, 5, []), (4, 0, [])], [9], [10], 1),
+    (15, 6): (5, 2, [(14, 10, []), (9, 5, []), (4, 0, [])], [8, 9], [10, 11], 1),
+    (16, 6): (5, 3, [(15, 13, [0, 1]), (12, 8, []), (7, 5, [0, 1]), (4, 0, [])], [5, 6, 7], [8, 9, 10], 2),
+    (10, 4): (4, 0, [(9, 8, [0, 1]), (7, 4, []), (3, 0, [])], [], [], 3),
+    (11, 4): (4, 0, [(10, 8, [0]), (7, 4, []), (3, 0, [])], [], [], 3),
+    (12, 4): (4, 0, [(11, 8, []), (7, 4, []), (3, 0, [])], [], [], 3),
+    (13, 4): (4, 0, [(12, 12, [0, 1, 2]), (11, 8, []), (7, 4, []), (3, 0, [])], [], [], 4),
+    (14, 4): (4, 1, [(13, 12, [0, 1]), (11, 8, []), (7, 4, []), (3, 0, [])], [6], [8], 2),
+    (15, 4): (4, 2, [(14, 12, [0]), (11, 8, []), (7, 4, []), (3, 0, [])], [5, 6], [8, 9], 2),
+    (16, 4): (4, 3, [(15, 12, []), (11, 8, []), (7, 4, []), (3, 0, [])], [5, 6, 7], [8, 9, 10], 2),
 }
 
 
 class Pass:
     def __init__(self, hi, lo, extras):
         self.hi, self.lo, self.extras = hi, lo, list(extras)
-        self.reg = list(range(lo, hi + 1)) + self.extras  # m bit j <-> position bit reg[j]
+        self.bits = list(range(lo, hi + 1))
+        self.reg = self.bits + self.extras  # m bit j <-> position bit reg[j]
         self.lanes = []
         self.warps = []
+        self.rank = []
+        self.phase = 0
+        self.sync_after = "block"  # exchange to the next pass (CT order): warp/block/cluster
 
 
-def local_map(L, rank):
-    """position bit -> local index bit (rank bits removed)."""
-    m, k = {}, 0
-    for b in range(L):
-        if b in rank:
-            continue
-        m[b] = k
-        k += 1
-    return m
+def swz(x):
+    """Padded shared-memory word of local index x."""
+    return x + (x >> 5) + (x >> 10) + (x >> 15)
 
 
-def choose_lanes(cands, lmaps, avoid_first=None):
-    """5 candidate bits whose local positions are distinct mod 5 in every
-    given layout (greedy from the front of `cands`)."""
+def free_bits(L, rank):
+    return [b for b in range(L) if b not in rank]
+
+
+# ----------------------------------------------------------------- lanes
+
+def lane_options(L, loge, logc, passes, rank0, rank1, split, pair=True):
+    """Per pass: its phase, rank bits, sync kind, and the candidate lane sets
+    (paired passes share the extra bit x)."""
     import itertools
-    for combo in itertools.combinations(cands, 5):
-        ok = True
-        for lm in lmaps:
-            if len({lm[b] % 5 for b in combo}) != 5:
-                ok = False
-                break
-        if ok:
-            return list(combo)
-    return None
+    n = len(passes)
+    phase = [0 if i < split else 1 for i in range(n)]
+    ranks = [rank0 if phase[i] == 0 else rank1 for i in range(n)]
+    thread_bits = []
+    for i, p in enumerate(passes):
+        tb = [b for b in range(L) if b not in p.reg and b not in ranks[i]]
+        assert len(tb) == L - logc - loge
+        thread_bits.append(tb)
+        p.rank = ranks[i]
+        p.phase = phase[i]
+        p.sync_after = "block"
+        if logc and i == split - 1:
+            p.sync_after = "cluster"
+    # pair passes (i, i+1) of the same phase whose groups fit the lanes:
+    # lanes(i) = bits(i+1) + x, lanes(i+1) = bits(i) + x, same warp bits
+    units = []  # (pass indices, list of candidate lane tuples per index)
+    i = 0
+    while i < n:
+        if pair and i + 1 < n:
+            a, b = passes[i], passes[i + 1]
+            if (phase[i] == phase[i + 1] and not a.extras and not b.extras
+                    and len(a.bits) == len(b.bits) and len(a.bits) <= 4):
+                common = sorted(x for x in thread_bits[i] if x in thread_bits[i + 1])
+                k = 5 - len(b.bits)
+                if len(common) >= k:
+                    cands = [(tuple(b.bits) + xs, tuple(a.bits) + xs) for xs in itertools.combinations(common, k)]
+                    units.append(((i, i + 1), cands))
+                    a.sync_after = "warp"
+                    i += 2
+                    continue
+        cands = [(c,) for c in itertools.combinations(sorted(thread_bits[i]), 5)]
+        units.append(((i,), cands))
+        i += 1
+    return units, thread_bits
 
 
-def build(L, loge, logc):
-    passes_spec, rank0, rank1, split = CONFIGS[(L, loge, logc)]
-    E = 1 << loge
-    local_bits = L - logc
-    logt = local_bits - loge
+# ------------------------------------------------------- local bit orders
+
+def access_sets(L, logc, passes, split):
+    """(phase, lane bits, fixed, remote) of every shared-memory access
+    pattern; `fixed` accesses keep their lane order (the cooperative
+    stages), the lane order of passes is free; `remote` marks the stores
+    of the phase change into another CTA's shared memory."""
+    sets = []
+    for i, p in enumerate(passes):
+        sets.append((p.phase, p, False, False))
+        if logc and p.sync_after == "cluster":
+            sets.append((1 - p.phase, p, False, True))  # CT: remote write into the next phase
+        if logc and i == split:
+            sets.append((0, p, False, True))  # GS: pass `split` writes into phase 0
+    sets.append((passes[0].phase, coop_lanes(L, passes[0].rank, True), True, False))
+    sets.append((passes[-1].phase, coop_lanes(L, passes[-1].rank, False), True, False))
+    return sets
+
+
+def solve_orders(L, rank0, rank1, sets, passes):
+    """Per phase, give the non-rank bits local indices (residues mod 5) so
+    that every access varies 5 bits of distinct residues; then list the
+    lanes of every pass in residue order.
+
+    Within a residue class the slot is free (only residues decide banks).
+    The lanes of the remote store into a phase take the lowest slot of
+    their classes, i.e. local indices 0..4: a warp's distributed-shared-
+    memory store then covers 32 consecutive words (4-5 sectors) instead of
+    up to 32 scattered sectors."""
+    out = {}
+    for ph, rank in ((0, rank0), (1, rank1)):
+        bits = free_bits(L, rank)
+        nloc = len(bits)
+        cap = [len([i for i in range(nloc) if i % 5 == r]) for r in range(5)]
+        groups, pinned, first = [], {}, []
+        for s_ph, acc, fixed, remote in sets:
+            if s_ph != ph:
+                continue
+            lanes = acc if fixed else acc.lanes
+            for b in lanes:
+                assert b not in rank, ("lane on a rank bit", L, ph)
+            groups.append(list(lanes))
+            if remote:
+                first += [b for b in lanes if b not in first]
+        involved = sorted({b for g in groups for b in g}, key=lambda b: -sum(b in g for g in groups))
+        res = dict(pinned)
+        used = [0] * 5
+        for b, r in res.items():
+            used[r] += 1
+
+        def ok(b, r):
+            if used[r] >= cap[r]:
+                return False
+            for g in groups:
+                if b in g and any(res.get(x) == r for x in g if x != b):
+                    return False
+            return True
+
+        def bt(k):
+            if k == len(involved):
+                return True
+            b = involved[k]
+            if b in res:
+                return bt(k + 1)
+            for r in range(5):
+                if ok(b, r):
+                    res[b] = r
+                    used[r] += 1
+                    if bt(k + 1):
+                        return True
+                    used[r] -= 1
+                    del res[b]
+            return False
+
+        if not bt(0):
+            return None
+        slots = {r: [i for i in range(nloc) if i % 5 == r] for r in range(5)}
+        order = {}
+        for b in first + sorted(b for b in res if b not in first):
+            order[b] = slots[res[b]].pop(0)
+        rest = sorted(i for r in range(5) for i in slots[r])
+        for b in bits:
+            if b not in order:
+                order[b] = rest.pop(0)
+        assert sorted(order.values()) == list(range(nloc))
+        out[ph] = order
+    # lane order of each pass: residue j on lane j in its own phase
+    for p in passes:
+        o = out[p.phase]
+        p.lanes = sorted(p.lanes, key=lambda b: o[b] % 5)
+    return out
+
+
+def coop_lanes(L, rank, nat):
+    """Lane bits (as position bits) of the cooperative global stages: thread
+    tid moves natural-order elements 2*tid (+ j*2T), i.e. its lanes vary
+    element-index bits 1..5."""
+    mirrored = [L - 1 - b for b in rank]
+    free_nat = [b for b in range(L) if b not in (rank if nat else mirrored)]
+    lane_nat = free_nat[1:6]
+    return lane_nat if nat else [L - 1 - b for b in lane_nat]
+
+
+def build(L, variant):
+    loge, logc, passes_spec, rank0, rank1, split = CONFIGS[(L, variant)]
+    logt = L - logc - loge
     assert logt >= 5, (L, loge, logc)
     passes = [Pass(*p) for p in passes_spec]
     assert len(rank0) == logc and len(rank1) == logc
-    # every bit processed exactly once, high to low
     seen = []
     for p in passes:
         assert p.hi >= p.lo and p.hi - p.lo + 1 + len(p.extras) == loge, (L, p.hi, p.lo)
@@ -108,45 +251,34 @@ def build(L, loge, logc):
         for x in p.extras:
             assert x < p.lo, "extra register bits must lie below the pass"
     assert seen == list(range(L - 1, -1, -1)), seen
-    n = len(passes)
-    for i, p in enumerate(passes):
-        rank = rank0 if i < split else rank1
-        for b in rank:
-            assert b not in p.reg, (L, i, b)
-        thread_bits = [b for b in range(L) if b not in p.reg and b not in rank]
-        assert len(thread_bits) == logt
-        lm_here = local_map(L, rank)
-        layouts = [lm_here]
-        if logc and i == split - 1:
-            layouts.append(local_map(L, rank1))  # remote write lands in phase-1 layout
-        if i == 0:
-            lanes = sorted(thread_bits)[:5]
-        elif i == n - 1:
-            lanes = sorted(thread_bits, reverse=True)[:5]
-        else:
-            lanes = choose_lanes(sorted(thread_bits), layouts)
-        assert lanes is not None, (L, i)
-        p.lanes = lanes
-        p.warps = [b for b in sorted(thread_bits) if b not in lanes]
-        p.rank = rank
-    check(L, loge, logc, passes, split)
-    check_coop(L, loge, logc, passes, split)
-    return dict(L=L, loge=loge, logc=logc, logt=logt, passes=passes, split=split,
-                rank0=rank0, rank1=rank1)
+    import itertools
+    orders = None
+    for pair in (True, False):  # warp-local exchanges where a layout allows them
+        units, thread_bits = lane_options(L, loge, logc, passes, rank0, rank1, split, pair)
+        for tries, choice in enumerate(itertools.product(*[c for _, c in units])):
+            for (idx, _), lanes in zip(units, choice):
+                for i, ln in zip(idx, lanes):
+                    passes[i].lanes = list(ln)
+                    passes[i].warps = [x for x in sorted(thread_bits[i]) if x not in ln]
+            orders = solve_orders(L, rank0, rank1, access_sets(L, logc, passes, split), passes)
+            if orders is not None or tries > 20000:
+                break
+        if orders is not None:
+            break
+    assert orders is not None, ("no bank-conflict-free schedule", L, loge, logc)
+    s = dict(L=L, variant=variant, loge=loge, logc=logc, logt=logt, passes=passes, split=split,
+             rank0=rank0, rank1=rank1, orders=orders)
+    check(s)
+    return s
 
 
-def swz(x):
-    """Padded shared-memory word of local index x: one pad word per 32, per
-    1024 and per 32768 words.  Additive over disjoint bit sets, so a word of
-    (thread bits | register bits) is thread base + a compile-time offset."""
-    return x + (x >> 5) + (x >> 10) + (x >> 15)
+# ----------------------------------------------------------------- checks
+
+def local_index(p, order):
+    return sum(((p >> b) & 1) << k for b, k in order.items())
 
 
-def compress(p, lm):
-    return sum(((p >> b) & 1) << k for b, k in lm.items())
-
-
-def positions(L, ps, rank_val, t, m):
+def positions(ps, rank_val, t, m):
     p = 0
     for j, b in enumerate(ps.reg):
         p |= ((m >> j) & 1) << b
@@ -159,64 +291,83 @@ def positions(L, ps, rank_val, t, m):
     return p
 
 
-def check(L, loge, logc, passes, split):
-    """Bijectivity, in-CTA ownership and conflict-free shared-memory access."""
-    E, C, T = 1 << loge, 1 << logc, 1 << (L - logc - loge)
+def conflict_free(addrs):
+    """32 word addresses of one warp access hit 32 distinct banks (32-bit
+    words).  64-bit words (the q >= 2^31 path) may see 2-way conflicts."""
+    return len({a & 31 for a in addrs}) == 32
+
+
+def check(s):
+    """Bijectivity, warp-locality of paired exchanges, conflict-free shared
+    memory for every access, and coverage of the cooperative stages."""
+    L, loge, logc, passes, split = s["L"], s["loge"], s["logc"], s["passes"], s["split"]
+    E, C, T = 1 << loge, 1 << logc, 1 << s["logt"]
+    orders = s["orders"]
     for i, ps in enumerate(passes):
         covered = set()
         for r in range(C):
             for t in range(T):
                 for m in range(E):
-                    covered.add(positions(L, ps, r, t, m))
+                    covered.add(positions(ps, r, t, m))
         assert len(covered) == 1 << L, ("not a bijection", L, i)
-        rank = ps.rank
-        layouts = [local_map(L, rank)]
-        if logc and i == split - 1:
-            layouts.append(local_map(L, passes[split].rank))
-        for lm in layouts:
+        layouts = [(orders[ps.phase], False)]
+        if logc and ps.sync_after == "cluster":
+            layouts.append((orders[1 - ps.phase], True))
+        if logc and i == split:
+            layouts.append((orders[0], True))
+        for order, remote in layouts:
             for w in range(min(T // 32, 4)):
                 for m in range(E):
-                    banks = {swz(compress(positions(L, ps, 0, w * 32 + l, m), lm)) & 31 for l in range(32)}
-                    assert len(banks) == 32, ("bank conflict", L, loge, i)
+                    addrs = [swz(local_index(positions(ps, 0, w * 32 + l, m), order)) for l in range(32)]
+                    assert conflict_free(addrs), ("bank conflict", L, loge, i)
+                    if remote:  # 32 consecutive 4-byte words: at most 5 32-byte sectors
+                        assert len({a >> 3 for a in addrs}) <= 5, ("scattered remote store", L, loge, i)
+        if ps.sync_after == "warp":
+            nxt = passes[i + 1]
+            for r in range(C):
+                for w in range(T // 32):
+                    wrote = {positions(ps, r, w * 32 + l, m) for l in range(32) for m in range(E)}
+                    read = {positions(nxt, r, w * 32 + l, m) for l in range(32) for m in range(E)}
+                    assert wrote == read, ("exchange leaves the warp", L, loge, i)
+    check_coop(s)
 
 
-def check_coop(L, loge, logc, passes, split):
-    """The cooperative HBM <-> shared-memory stages: thread tid, iteration j
-    moves natural indices k, k+1 (k = natural(2*tid + 2*j*T)).  Check that
-    every owned coefficient is moved once and that the two 32-bit shared
-    accesses of a warp hit 32 distinct banks."""
-    C, T = 1 << logc, 1 << (L - logc - loge)
+def check_coop(s):
+    L, loge, logc, passes = s["L"], s["loge"], s["logc"], s["passes"]
+    C, T = 1 << logc, 1 << s["logt"]
     local = 1 << (L - logc)
-    for phase_pass, nat in ((passes[0], True), (passes[-1], False),
-                            (passes[-1], True), (passes[0], False)):
-        rank = phase_pass.rank
-        lm = local_map(L, rank)
+    for ps, nat in ((passes[0], True), (passes[-1], False)):
+        rank = ps.rank
+        order = s["orders"][ps.phase]
         mirrored = [L - 1 - b for b in rank]
         free_nat = [b for b in range(L) if b not in (rank if nat else mirrored)]
         for r in range(C):
             seen = set()
             for j in range(local // (2 * T)):
                 for w in range(T // 32):
-                    banks = [set(), set()]
+                    addrs = [[], []]
                     for lane in range(32):
                         i = 2 * (w * 32 + lane) + 2 * j * T
                         for e in range(2):
-                            k = sum(((i + e) >> n & 1) << b for n, b in enumerate(free_nat))
+                            k = sum((((i + e) >> n) & 1) << b for n, b in enumerate(free_nat))
                             rb = rank if nat else mirrored
                             k |= sum(((r >> n) & 1) << b for n, b in enumerate(rb))
                             p = k if nat else int(format(k, f"0{L}b")[::-1], 2)
                             seen.add(p)
-                            banks[e].add(swz(compress(p, lm)) & 31)
-                    assert all(len(bk) == 32 for bk in banks), ("coop bank conflict", L, loge, nat)
+                            addrs[e].append(swz(local_index(p, order)))
+                    assert all(conflict_free(a) for a in addrs), ("coop bank conflict", L, loge, nat)
             owned = {p for p in range(1 << L)
                      if all(((p >> b) & 1) == ((r >> n) & 1) for n, b in enumerate(rank))}
             assert seen == owned, ("coop coverage", L, loge, nat)
 
 
+# ------------------------------------------------------------------- emit
+
 def emit(scheds):
     out = ["// Generated by gen_schedule.py -- pass schedules of the fast NTT kernels.",
            "// Do not edit by hand: change CONFIGS in gen_schedule.py and rerun it.",
            "#pragma once", "", "namespace bc {", "namespace fast {", "",
+           "enum SyncKind { kSyncWarp = 0, kSyncBlock = 1, kSyncCluster = 2 };", "",
            "struct PassDesc {",
            "    int hi, lo;       // processed position bits (inclusive)",
            "    int nreg;         // register bits: hi-lo+1 processed, then extras",
@@ -225,11 +376,13 @@ def emit(scheds):
            "    int nwarp;",
            "    int warp[10];     // warp index bit j <-> position bit warp[j]",
            "    int phase;        // 0 or 1 (which rank bits the CTA owns)",
+           "    int sync_after;   // exchange with the next pass in CT order (SyncKind)",
            "};", "",
-           "struct RankBits {",
-           "    int b[3];",
+           "struct BitTable {",
+           "    int b[18];",
            "};", "",
-           "template <int L, int LOGE> struct Sched;", ""]
+           "template <int L, int V> struct Sched;", ""]
+    sync = {"warp": 0, "block": 1, "cluster": 2}
     for s in scheds:
         L, loge, logc = s["L"], s["loge"], s["logc"]
         ps = s["passes"]
@@ -237,20 +390,41 @@ def emit(scheds):
         def arr(v, n):
             v = list(v) + [0] * (n - len(v))
             return "{" + ", ".join(str(x) for x in v) + "}"
-        out.append(f"template <> struct Sched<{L}, {loge}> {{")
-        out.append(f"    static constexpr int kLogC = {logc}, kLogT = {s['logt']}, kPasses = {len(ps)}, "
+
+        def order_table(ph):
+            o = s["orders"][ph]
+            return arr([o.get(b, -1) for b in range(L)], 18)
+        out.append(f"template <> struct Sched<{L}, {s['variant']}> {{")
+        out.append(f"    static constexpr int kLogE = {loge}, kLogC = {logc}, kLogT = {s['logt']}, kPasses = {len(ps)}, "
                    f"kSplit = {s['split']};")
-        out.append(f"    __host__ __device__ static constexpr int rank0(int j) {{ return RankBits{arr(s['rank0'], 3)}.b[j]; }}")
-        out.append(f"    __host__ __device__ static constexpr int rank1(int j) {{ return RankBits{arr(s['rank1'], 3)}.b[j]; }}")
+        out.append(f"    __host__ __device__ static constexpr int rank0(int j) {{ return BitTable{{{arr(s['rank0'], 18)}}}.b[j]; }}")
+        out.append(f"    __host__ __device__ static constexpr int rank1(int j) {{ return BitTable{{{arr(s['rank1'], 18)}}}.b[j]; }}")
+        out.append("    // local bit index of position bit b in phase 0 / 1 (-1: a rank bit)")
+        out.append(f"    __host__ __device__ static constexpr int local0(int b) {{ return BitTable{{{order_table(0)}}}.b[b]; }}")
+        out.append(f"    __host__ __device__ static constexpr int local1(int b) {{ return BitTable{{{order_table(1)}}}.b[b]; }}")
         out.append("    __host__ __device__ static constexpr PassDesc pass(int i) {")
         for i, p in enumerate(ps):
-            ph = 0 if i < s["split"] else 1
             out.append(f"        if (i == {i}) return PassDesc{{{p.hi}, {p.lo}, {len(p.reg)}, {arr(p.reg, 5)}, "
-                       f"{arr(p.lanes, 5)}, {len(p.warps)}, {arr(p.warps, 10)}, {ph}}};")
+                       f"{arr(p.lanes, 5)}, {len(p.warps)}, {arr(p.warps, 10)}, {p.phase}, {sync[p.sync_after]}}};")
         out.append("        return PassDesc{};")
         out.append("    }")
         out.append("};")
         out.append("")
+    out.append("// hi bit of the pass that processes position bit b in schedule (L, V)")
+    out.append("__host__ __device__ constexpr int sched_pass_hi(int L, int V, int b) {")
+    for s in scheds:
+        conds = " : ".join(f"b >= {p.lo} ? {p.hi}" for p in s["passes"])
+        out.append(f"    if (L == {s['L']} && V == {s['variant']}) return {conds} : -1;")
+    out.append("    return -1;")
+    out.append("}")
+    out.append("")
+    out.append("// log2 of the cluster size of schedule (L, V); -1 if there is none")
+    out.append("__host__ __device__ constexpr int sched_logc(int L, int V) {")
+    for s in scheds:
+        out.append(f"    if (L == {s['L']} && V == {s['variant']}) return {s['logc']};")
+    out.append("    return -1;")
+    out.append("}")
+    out.append("")
     out += ["}  // namespace fast", "}  // namespace bc", ""]
     return "\n".join(out)
 
@@ -260,9 +434,13 @@ def all_schedules():
 
 
 def main():
-    text = emit(all_schedules())
+    scheds = all_schedules()
+    for s in scheds:
+        kinds = [p.sync_after for p in s["passes"][:-1]]
+        print(f"L={s['L']:2d} V={s['variant']} E={1 << s['loge']:2d} C={1 << s['logc']} T={1 << s['logt']}: "
+              f"exchanges {kinds}")
     with open(OUT, "w") as f:
-        f.write(text)
+        f.write(emit(scheds))
     print("wrote", OUT)
 
 
