@@ -189,6 +189,44 @@ int bc_pointwise_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, ui
 int bc_polymul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                uint32_t batch, const bc_layout *layout, void *stream);
 
+/* Largest batch * n_limbs * N that bc_polymul_static_scratch accepts above
+ * the fused size (2^21 coefficients per operand; the buffer is 32 MiB). */
+#define BC_POLYMUL_STATIC_MAX_COEFFS (1u << 21)
+
+/* bc_polymul that never allocates device memory.  No counterpart in the
+ * reference: FheFastPolyMul::execute (ops/fhe_fast_poly_mul.rs:122)
+ * allocates its intermediates and output on every call.
+ *
+ * Who needs it: above the fused size (N > 2^14 for moduli below 2^31,
+ * N > 2^13 otherwise) bc_polymul allocates a temporary device buffer,
+ * synchronizes the stream and frees the buffer on every call.  A caller
+ * cannot afford that when the device memory is already reserved by another
+ * allocator (a framework's caching pool leaves cudaMalloc nothing to hand
+ * out), or when it keeps work in flight on several streams and cudaFree's
+ * implicit device-wide synchronization would stall them.  This entry point
+ * keeps the temporary in one fixed buffer per device in the library's static
+ * device memory instead.  It computes the same result as bc_polymul and
+ * neither allocates nor synchronizes.
+ *
+ * Limits: above the fused size, batch * n_limbs * N must not exceed
+ * BC_POLYMUL_STATIC_MAX_COEFFS, and `layout` must be NULL or the default
+ * compact layout.  Larger or strided calls fail with BC_ERR_INVALID_INPUT /
+ * BC_ERR_UNSUPPORTED before any work is queued.  At fused sizes it is
+ * bc_polymul and has no size limit.
+ *
+ * Sharing: every call on a GPU uses the same buffer.  Calls on one stream
+ * are ordered and safe.  Calls that overlap in time race on the buffer and
+ * give wrong results: other streams, other host threads, other plans or
+ * contexts on the same GPU.  The caller must serialize them.
+ *
+ * Set-up: the first call on each device looks up the buffer's device
+ * address, which may make the driver load the library's device code.  Make
+ * that first call before any stream capture.  Nothing in the buffer needs
+ * to start at zero: every word is written before it is read. */
+int bc_polymul_static_scratch(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b,
+                              uint64_t *d_c, uint32_t batch, const bc_layout *layout,
+                              void *stream);
+
 /* Seeded synthetic coefficients, uniform in [0, q_l): element (l, p, j) of
  * the batch gets value(seed, ((l * total_polys + first_poly + p) * N + j)),
  * value(s, g) = floor(splitmix64(s + (g + 1) * 0x9E3779B97F4A7C15) * q / 2^64). */
