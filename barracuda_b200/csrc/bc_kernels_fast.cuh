@@ -483,14 +483,24 @@ struct Step {
                                  : (GS ? S::pass(PI - 1).sync_after : P.sync_after);
     // Stage (within this pass) that carries N^-1: the very last stage.
     static constexpr int kScaleStage = (SCALE && STEP == NSTEP - 1) ? R - 1 : -1;
+    // Twiddle chunks in flight ahead of the butterflies; the ring has the
+    // same shape in every pass of a schedule.
+    static constexpr int kAhead = E >= 32 ? 1 : 2;
+    using Ring = typename A::Tw[kAhead + 1][TwSeq<A, S, PI, GS>::kCh];
+
+    // Issues this pass's first twiddle chunks.  Called by the previous pass
+    // (or the kernel) before the barrier that precedes this pass, so their
+    // L2 latency overlaps the barrier wait.
+    __device__ __forceinline__ static void prefetch(Ring &ring, const typename A::Tw *tw, uint32_t rank) {
+        const uint32_t h = thread_pos<S, PI>(threadIdx.x, rank) >> (P.hi + 1);
+        prefetch_chunks<A, S, L, PI, GS, kAhead, 0>(ring, tw, h);
+    }
 
     __device__ __forceinline__ static void run(W *smem, const typename A::Tw *tw, const LimbConst &lc,
-                                               uint32_t rank) {
+                                               uint32_t rank, Ring &ring) {
+        using Next = Step<A, L, LOGE, GS, SCALE, (STEP + 1 < NSTEP ? STEP + 1 : STEP)>;
         const uint32_t tp = thread_pos<S, PI>(threadIdx.x, rank);
         const uint32_t h = tp >> (P.hi + 1);  // group-index bits above the pass
-        constexpr int kAhead = E >= 32 ? 1 : 2;
-        typename A::Tw ring[kAhead + 1][TwSeq<A, S, PI, GS>::kCh];
-        prefetch_chunks<A, S, L, PI, GS, kAhead, 0>(ring, tw, h);
         W v[E];
         {
             const uint32_t at = smem_addr<S, L>(tp, P.phase);
@@ -521,6 +531,7 @@ struct Step {
                 const uint32_t off = smem_addr<S, L>(p, nphase);
                 st_cluster<W>(map_rank(base + off * sizeof(W), dest), v[m]);
             }
+            if constexpr (STEP + 1 < NSTEP) Next::prefetch(ring, tw, rank);
             cluster_sync_all();
         } else {
             // ---- back to shared memory, same layout.  The base goes through
@@ -530,13 +541,14 @@ struct Step {
             pin(at);
 #pragma unroll
             for (int m = 0; m < E; ++m) smem[at + smem_addr<S, L>(reg_pos<S, PI>(m), P.phase)] = v[m];
+            if constexpr (STEP + 1 < NSTEP) Next::prefetch(ring, tw, rank);
             // warp-local exchange: the next pass reads only what this warp wrote
             if constexpr (kSync == kSyncWarp)
                 __syncwarp();
             else
                 __syncthreads();
         }
-        if constexpr (STEP + 1 < NSTEP) Step<A, L, LOGE, GS, SCALE, STEP + 1>::run(smem, tw, lc, rank);
+        if constexpr (STEP + 1 < NSTEP) Next::run(smem, tw, lc, rank, ring);
     }
 };
 
@@ -557,6 +569,7 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, PF>
     // CT reads natural order, GS reads bit-reversed positions
     using In = Coop<A, S, L, Sh::kT, Sh::kLocal, ph_in, !GS>;
     using Out = Coop<A, S, L, Sh::kT, Sh::kLocal, ph_out, GS>;
+    using First = Step<A, L, LOGE, GS, SCALE, 0>;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     W *work = reinterpret_cast<W *>(smem_raw);
     uint64_t *stage = reinterpret_cast<uint64_t *>(smem_raw + Sm::kWorkBytes);
@@ -577,8 +590,10 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, PF>
         if constexpr (A::kBits == 32) {
             if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) atomicOr(a.status, kStatusInputRange);
         }
+        typename First::Ring ring;
+        First::prefetch(ring, tw, rank);
         __syncthreads();
-        Step<A, L, LOGE, GS, SCALE, 0>::run(work, tw, lc, rank);
+        First::run(work, tw, lc, rank, ring);
         Out::store(work, a.out + base_of(cl), rank, lc);
         return;
     }
@@ -590,8 +605,10 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, PF>
         cp_async_wait_all();
         In::convert(stage, work, rank, lc, bad);
         if (cl + G < npolys) In::prefetch(stage, a.in + base_of(cl + G), rank);
+        typename First::Ring ring;
+        First::prefetch(ring, tw, rank);
         __syncthreads();
-        Step<A, L, LOGE, GS, SCALE, 0>::run(work, tw, lc, rank);
+        First::run(work, tw, lc, rank, ring);
         Out::store(work, a.out + base_of(cl), rank, lc);
         __syncthreads();
     }

@@ -23,12 +23,13 @@ a pass are listed in residue order.  The guarantee is for 32-bit words: the
 over disjoint bit sets, so every access is a per-thread base plus a
 compile-time offset.
 
-Lanes and warps: when two consecutive passes of a phase process bit groups
-GA and GB, the first pass puts GB (plus one common bit x) in its lanes and
-the second puts GA (plus x) in its lanes; both keep the same warp bits, so
-the data they exchange never leaves a warp and the pass boundary needs only
-__syncwarp().  Passes that cannot be paired that way exchange through the
-whole CTA (__syncthreads()).
+Lanes and warps: when pass B follows pass A in the same phase, the first
+puts the register bits that B adds in its lanes and the second puts the
+register bits that A drops in its lanes (both plus common bits x, when fewer
+than five bits change); both keep the same warp bits, so the data they
+exchange never leaves a warp and the pass boundary needs only __syncwarp().
+Passes that cannot be paired that way exchange through the whole CTA
+(__syncthreads()).
 
 Global memory is read and written by separate cooperative stages (16-byte
 accesses of coefficient pairs in natural order), whose shared-memory
@@ -112,19 +113,23 @@ def lane_options(L, loge, logc, passes, rank0, rank1, split, pair=True):
         p.sync_after = "block"
         if logc and i == split - 1:
             p.sync_after = "cluster"
-    # pair passes (i, i+1) of the same phase whose groups fit the lanes:
-    # lanes(i) = bits(i+1) + x, lanes(i+1) = bits(i) + x, same warp bits
+    # pair passes (i, i+1) of the same phase: the register bits that pass
+    # i+1 adds (new_b) are lanes of pass i, the ones it drops (new_a) are
+    # lanes of pass i+1, both keep the same warp bits and share the other
+    # lanes xs -- then the data they exchange never leaves a warp.
     units = []  # (pass indices, list of candidate lane tuples per index)
     i = 0
     while i < n:
         if pair and i + 1 < n:
             a, b = passes[i], passes[i + 1]
-            if (phase[i] == phase[i + 1] and not a.extras and not b.extras
-                    and len(a.bits) == len(b.bits) and len(a.bits) <= 4):
+            new_b = [x for x in b.reg if x not in a.reg]
+            new_a = [x for x in a.reg if x not in b.reg]
+            if (phase[i] == phase[i + 1] and len(new_b) == len(new_a) <= 5
+                    and all(x in thread_bits[i] for x in new_b)):
                 common = sorted(x for x in thread_bits[i] if x in thread_bits[i + 1])
-                k = 5 - len(b.bits)
+                k = 5 - len(new_b)
                 if len(common) >= k:
-                    cands = [(tuple(b.bits) + xs, tuple(a.bits) + xs) for xs in itertools.combinations(common, k)]
+                    cands = [(tuple(new_b) + xs, tuple(new_a) + xs) for xs in itertools.combinations(common, k)]
                     units.append(((i, i + 1), cands))
                     a.sync_after = "warp"
                     i += 2

@@ -52,8 +52,11 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks, power and throttle reasons sampled during the timed region:
+    NVML polled every 10 ms from a thread (the timed region can be shorter
+    than nvidia-smi's sampling period), nvidia-smi -lms 200 if NVML fails."""
 
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -62,8 +65,42 @@ class ClockSampler:
         self.gpu = gpu
         self.proc = None
         self.path = None
+        self.thread = None
+        self.rows = []
+        self.done = False
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.gpu)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def start(self):
+        import threading
+        import time
+        try:
+            nv, h = self._nvml_handle()
+            bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+            smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+
+            def poll():
+                while not self.done:
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), smax,
+                                      nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                      [n for n, b in zip(self.NAMES, bits) if r & b]))
+                    time.sleep(0.01)
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
@@ -75,32 +112,32 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        rows = []
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9 and parts[1].isdigit():
-                rows.append(parts)
-        os.unlink(self.path)
+        if self.thread is not None:
+            self.done = True
+            self.thread.join(timeout=5)
+            rows, source = self.rows, "nvml, 10 ms"
+        elif self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            rows, source = [], "nvidia-smi, 200 ms"
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    pw = float(parts[3]) if parts[3].replace(".", "", 1).isdigit() else 0.0
+                    rows.append((int(parts[1]), int(parts[2]), pw,
+                                 [n for n, v in zip(self.NAMES, parts[5:9]) if v.lower().startswith("active")]))
+            os.unlink(self.path)
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"]}
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [int(r[1]) for r in rows]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for nm, v in zip(names, r[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]),
-                "power_w_max": max(float(r[3]) for r in rows if r[3].replace('.', '', 1).isdigit())
-                if any(r[3].replace('.', '', 1).isdigit() for r in rows) else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
+                "power_w_max": max(r[2] for r in rows),
+                "reasons": sorted({n for r in rows for n in r[3]}), "samples": len(rows),
+                "source": source}
 
 
 def dist_setup():
