@@ -3,8 +3,8 @@
 The product is libbarracuda_fhe.so (C ABI: include/barracuda_fhe.h).  This
 package builds it in-tree (``barracuda_b200.build``), binds it with ctypes
 (``_native``) and mirrors the reference op API (``ops``) and the batched plan
-API (``plan``) on top of it.  There is no CPU fallback: without the library
-every call raises.
+API (``plan``) on top of it, and splits a job over GPUs (``shard``).  There is
+no CPU fallback: without the library every call raises.
 """
 from ._native import BarracudaError, NativeLibraryMissing, LIB_PATH  # noqa: F401
 from .ops import (  # noqa: F401
@@ -14,3 +14,4 @@ from .ops import (  # noqa: F401
 from .plan import (  # noqa: F401
     NttPlan, Layout, CYCLIC, NEGACYCLIC, ntt_prime, ntt_primes, negacyclic_root, partition, digest,
 )
+from .shard import Shard, ShardGroup, ShardFailure, job_digest  # noqa: F401

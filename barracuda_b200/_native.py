@@ -112,7 +112,7 @@ SIGNATURES = {
     "bc_polymul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_polymul_static_scratch": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_fill_uniform": (_i32, [_vp, _vp, _u32, _lay, _u64, _u64, _u64, _vp]),
-    "bc_digest": (_i32, [_vp, _vp, _sz, _vp, _vp]),
+    "bc_digest": (_i32, [_vp, _vp, _sz, _u64, _vp, _vp]),
     "bc_partition": (_i32, [_u64, _u32, _u32, _u64p, _u64p]),
     "bc_ntt_prime": (_u64, [_u32, _u32, _u32]),
     "bc_negacyclic_root": (_u64, [_u64, _u32]),

@@ -78,6 +78,6 @@ int launch_scale(Word w, const KArgs &a, cudaStream_t s);
 
 int launch_fill_uniform(const KArgs &a, uint64_t seed, uint64_t first_poly,
                         uint64_t total_polys, cudaStream_t s);
-int launch_digest(const uint64_t *in, size_t count, uint64_t *out, cudaStream_t s);
+int launch_digest(const uint64_t *in, size_t count, uint64_t first, uint64_t *out, cudaStream_t s);
 
 }  // namespace bc

@@ -313,11 +313,11 @@ __global__ void k_fill_uniform(KArgs a, uint64_t seed, uint64_t first_poly, uint
     }
 }
 
-__global__ void k_digest(const uint64_t *in, size_t count, uint64_t *out) {
+__global__ void k_digest(const uint64_t *in, size_t count, uint64_t first, uint64_t *out) {
     uint64_t acc = 0;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count;
          i += static_cast<size_t>(gridDim.x) * blockDim.x)
-        acc += splitmix64(in[i] ^ (i * 0xD1B54A32D192ED03ull));
+        acc += splitmix64(in[i] ^ ((first + i) * 0xD1B54A32D192ED03ull));
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if ((threadIdx.x & 31) == 0) atomicAdd(reinterpret_cast<unsigned long long *>(out), acc);
 }
@@ -471,9 +471,9 @@ int launch_fill_uniform(const KArgs &a, uint64_t seed, uint64_t first_poly, uint
     return check_launch("k_fill_uniform");
 }
 
-int launch_digest(const uint64_t *in, size_t count, uint64_t *out, cudaStream_t s) {
+int launch_digest(const uint64_t *in, size_t count, uint64_t first, uint64_t *out, cudaStream_t s) {
     cudaMemsetAsync(out, 0, sizeof(uint64_t), s);
-    k_digest<<<grid_for(count, 256), 256, 0, s>>>(in, count, out);
+    k_digest<<<grid_for(count, 256), 256, 0, s>>>(in, count, first, out);
     return check_launch("k_digest");
 }
 

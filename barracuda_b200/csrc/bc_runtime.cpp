@@ -683,11 +683,13 @@ int bc_fill_uniform(bc_plan *p, uint64_t *out, uint32_t batch, const bc_layout *
     return launch_fill_uniform(a, seed, first_poly, total_polys, pick_stream(p, stream));
 }
 
-int bc_digest(bc_ctx *ctx, const uint64_t *in, size_t count, uint64_t *out, void *stream) {
+int bc_digest(bc_ctx *ctx, const uint64_t *in, size_t count, uint64_t first_index, uint64_t *out,
+              void *stream) {
     if (!ctx || !out || (!in && count)) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
     int st = use_device(ctx);
     if (st) return st;
-    return launch_digest(in, count, out, stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
+    return launch_digest(in, count, first_index, out,
+                         stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
 }
 
 int bc_partition(uint64_t units, uint32_t shards, uint32_t shard, uint64_t *begin, uint64_t *count) {

@@ -129,5 +129,5 @@ class NttPlan:
             pass
 
 
-def digest(device: Device, buf, count: int, out, stream: int = 0):
-    check(lib().bc_digest(device.handle, _ptr(buf), count, _ptr(out), stream or None))
+def digest(device: Device, buf, count: int, out, stream: int = 0, first_index: int = 0):
+    check(lib().bc_digest(device.handle, _ptr(buf), count, first_index, _ptr(out), stream or None))

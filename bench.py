@@ -215,37 +215,49 @@ def cpu_baseline_sample(seconds_target=12.0):
 
 def run_ours(args):
     import torch
-    import torch.distributed as dist
 
     import barracuda_b200 as bc
 
     world, rank, local = dist_setup()
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
-    dev = bc.Device(local)
+    # one process per GPU; the only collectives are the timing max, the unit
+    # count and the digest gather (NCCL), each preceded by a status check
+    group = bc.ShardGroup("nccl", timeout=300.0, device=torch.device("cuda", local))
+    try:
+        _run_ours(args, torch, bc, group, world, rank, local)
+    finally:
+        group.close()
 
+
+def _run_ours(args, torch, bc, group, world, rank, local):
+    dev = bc.Device(local)
     cts_total = args.cts_total if args.strong else args.cts * world
-    ct_begin, ct_count = bc.partition(cts_total, world, rank)
+    shard = bc.Shard.of(cts_total, world, rank)
+    ct_begin, ct_count = shard.begin, shard.count
     polys = 2 * ct_count
     qs = bc.ntt_primes(31, N, LIMBS)
     psis = [bc.negacyclic_root(q, N) for q in qs]
-    plan = bc.NttPlan(dev, N, qs, psis, mode=bc.NEGACYCLIC)
     lay = bc.Layout(limb_stride=N, poly_stride=LIMBS * N)
     words = polys * LIMBS * N
-    x = torch.empty(words, dtype=torch.int64, device="cuda")
-    X = torch.empty(words, dtype=torch.int64, device="cuda")
+    first_word = 2 * ct_begin * LIMBS * N  # global index of this shard's first coefficient
     # an explicit stream: handle 0 (torch's legacy default stream) would mean
     # "the context stream" to the C ABI, and the events must sit on the
     # stream the kernels run on
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     sh = stream.cuda_stream
-    plan.fill_uniform(x, polys, seed=0, first_poly=2 * ct_begin, total_polys=2 * cts_total,
-                      layout=lay, stream=sh)
-    dig = torch.zeros(2, dtype=torch.int64, device="cuda")
-    bc.digest(dev, x, words, dig[0:1], stream=sh)
+
+    def setup():
+        plan = bc.NttPlan(dev, N, qs, psis, mode=bc.NEGACYCLIC)
+        x = torch.empty(words, dtype=torch.int64, device="cuda")
+        X = torch.empty(words, dtype=torch.int64, device="cuda")
+        plan.fill_uniform(x, polys, seed=0, first_poly=2 * ct_begin, total_polys=2 * cts_total,
+                          layout=lay, stream=sh)
+        return plan, x, X
+
+    plan, x, X = group.step("setup", setup)
+    dig = torch.zeros(3, dtype=torch.int64, device="cuda")
+    bc.digest(dev, x, words, dig[0:1], stream=sh, first_index=first_word)
 
     def step(ev=None):
         if ev is not None:
@@ -260,8 +272,8 @@ def run_ours(args):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    group.step("warmup", lambda: None)
+    group.barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
@@ -274,27 +286,30 @@ def run_ours(args):
     t1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    if world > 1:
-        dist.barrier()
+    group.step("timed", lambda: None)
+    group.barrier()
     ms = t0.elapsed_time(t1)
     fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
     inv_ms = [e[1].elapsed_time(e[2]) for e in evs]
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    units = torch.tensor([2.0 * polys * LIMBS * args.steps], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(units, op=dist.ReduceOp.SUM)
-    ms_max = float(t.item())
-    value = float(units.item()) / (ms_max / 1000.0)
+    ms_max = group.max_f64(ms)
+    units = 2 * sum(r[0] for r in group.gather_u64([polys * LIMBS])) * args.steps
+    value = units / (ms_max / 1000.0)
 
-    # round trip must leave the inputs unchanged
-    bc.digest(dev, x, words, dig[1:2], stream=sh)
+    # verification: forward output and round trip, digests with global
+    # indices gathered to every rank (their sums do not depend on the split)
+    bc.digest(dev, X, words, dig[1:2], stream=sh, first_index=first_word)
+    bc.digest(dev, x, words, dig[2:3], stream=sh, first_index=first_word)
     torch.cuda.synchronize()
-    roundtrip_ok = bool(dig[0].item() == dig[1].item())
+    rows = group.gather_u64([int(v) for v in dig.tolist()])
+    verification = {
+        "input_digest": f"{bc.job_digest(r[0] for r in rows):016x}",
+        "forward_digest": f"{bc.job_digest(r[1] for r in rows):016x}",
+        "roundtrip_identity": all(r[0] == r[2] for r in rows),
+        "gathered": f"all_gather of per-rank digests over {world} rank(s)",
+    }
 
     # ---- e2e through the public API with pinned host buffers
-    e2e = (run_e2e(args, torch, bc, dev, plan, lay, polys, words, qs, x, X, rank, world, dist)
-           if args.e2e_steps > 0 else None)
+    e2e = (run_e2e(args, torch, plan, lay, polys, x, X, group) if args.e2e_steps > 0 else None)
 
     info = plan.info
     launches_per_transform = {0: 1, 1: 1, 2: N_LOG + 2, 3: 1}[info["kernel_kind"]]
@@ -324,7 +339,7 @@ def run_ours(args):
             "config": {"workload": "config3: N=2^16 negacyclic NTT+INTT, 48 limbs (largest primes "
                                    "< 2^31, q = 1 mod 2N), [ct][2][limb][N] u64 layout",
                        "cts_per_gpu": ct_count, "cts_total": cts_total, "limb_transforms_per_step":
-                       int(units.item() / args.steps), "l2": "inputs 6.4 GB/GPU > 126 MB L2, no flush",
+                       int(units / args.steps), "l2": "inputs 6.4 GB/GPU > 126 MB L2, no flush",
                        "parallelism": f"shard by ciphertext x{world}",
                        "kernel_kind": info["kernel_kind"], "cluster": info["cluster_size"]},
             "gb_per_s": value * BYTES_PER_TRANSFORM / 1e9,
@@ -333,18 +348,18 @@ def run_ours(args):
             "gpu_launches": 2 * launches_per_transform * args.steps,
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "roundtrip_identity": roundtrip_ok,
+            "roundtrip_identity": verification["roundtrip_identity"],
+            "verification": verification,
         }
         print(json.dumps(line), flush=True)
     plan.close()
     dev.close()
-    if world > 1:
-        dist.destroy_process_group()
 
 
-def run_e2e(args, torch, bc, dev, plan, lay, polys, words, qs, x, X, rank, world, dist):
+def run_e2e(args, torch, plan, lay, polys, x, X, group):
     """Host buffers in, host buffers out, through the same public calls."""
     steps = max(1, args.e2e_steps)
+    words = polys * LIMBS * N
     host = torch.empty(words, dtype=torch.int64, pin_memory=True)
     # inputs for e2e: the seeded data, staged once to pinned host memory
     host.copy_(x, non_blocking=False)
@@ -372,8 +387,8 @@ def run_e2e(args, torch, bc, dev, plan, lay, polys, words, qs, x, X, rank, world
 
     one_step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    group.step("e2e warmup", lambda: None)
+    group.barrier()
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
@@ -384,13 +399,11 @@ def run_e2e(args, torch, bc, dev, plan, lay, polys, words, qs, x, X, rank, world
             torch.cuda.current_stream().wait_stream(s)
     ev1.record()
     torch.cuda.synchronize()
-    secs = ev0.elapsed_time(ev1) / 1000.0
-    t = torch.tensor([secs], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    units = 2.0 * polys * LIMBS * steps * world
-    return {"value": units / float(t.item()), "unit": UNIT,
-            "h2d_bytes_per_step": words * 8, "d2h_bytes_per_step": words * 8,
+    secs = group.max_f64(ev0.elapsed_time(ev1) / 1000.0)
+    limb_polys = sum(r[0] for r in group.gather_u64([polys * LIMBS]))  # whole job
+    units = 2 * limb_polys * steps
+    return {"value": units / secs, "unit": UNIT,
+            "h2d_bytes_per_step": limb_polys * N * 8, "d2h_bytes_per_step": limb_polys * N * 8,
             "steps": steps, "chunks": chunks,
             "timing": "CUDA events around the copy/compute streams, max over ranks"}
 

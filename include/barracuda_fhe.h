@@ -232,9 +232,13 @@ int bc_polymul_static_scratch(bc_plan *plan, const uint64_t *d_a, const uint64_t
  * value(s, g) = floor(splitmix64(s + (g + 1) * 0x9E3779B97F4A7C15) * q / 2^64). */
 int bc_fill_uniform(bc_plan *plan, uint64_t *d_out, uint32_t batch, const bc_layout *layout,
                     uint64_t seed, uint64_t first_poly, uint64_t total_polys, void *stream);
-/* Order-sensitive 64-bit digest of `count` u64 words (for cross-GPU checks):
- * sum_i splitmix64(x_i ^ (i * 0xD1B54A32D192ED03)) mod 2^64, written to *d_out. */
-int bc_digest(bc_ctx *ctx, const uint64_t *d_in, size_t count, uint64_t *d_out, void *stream);
+/* Order-sensitive 64-bit digest of `count` u64 words for cross-GPU checks:
+ * sum_i splitmix64(x_i ^ ((first_index + i) * 0xD1B54A32D192ED03)) mod 2^64,
+ * written to *d_out.  With first_index = the global index of d_in[0], the
+ * digests of the shards of an array add up (mod 2^64) to the digest of the
+ * whole array, whatever the number of GPUs. */
+int bc_digest(bc_ctx *ctx, const uint64_t *d_in, size_t count, uint64_t first_index,
+              uint64_t *d_out, void *stream);
 
 /* ------------------------------------------------------- multi-GPU split */
 /* Contiguous balanced split of `units` over `shards`: shard s gets

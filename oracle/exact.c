@@ -245,3 +245,9 @@ uint64_t orc_seeded_value(uint64_t seed, uint64_t g, uint64_t q) {
 void orc_seeded_fill(uint64_t *out, size_t count, uint64_t seed, uint64_t g0, uint64_t q) {
     for (size_t i = 0; i < count; ++i) out[i] = orc_seeded_value(seed, g0 + i, q);
 }
+
+uint64_t orc_digest(const uint64_t *x, size_t count, uint64_t first_index) {
+    uint64_t acc = 0;
+    for (size_t i = 0; i < count; ++i) acc += splitmix(x[i] ^ ((first_index + i) * 0xD1B54A32D192ED03ull));
+    return acc;
+}

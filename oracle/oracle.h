@@ -109,6 +109,11 @@ void orc_negacyclic_convolution(const uint64_t *a, const uint64_t *b, uint64_t *
  * value(seed, g) = floor(splitmix64(seed + (g+1)*0x9E3779B97F4A7C15) * q / 2^64). */
 uint64_t orc_seeded_value(uint64_t seed, uint64_t g, uint64_t q);
 void orc_seeded_fill(uint64_t *out, size_t count, uint64_t seed, uint64_t g0, uint64_t q);
+/* Order-sensitive digest of the product's verification path (bc_digest):
+ * sum_i splitmix64(x_i ^ ((first_index + i) * 0xD1B54A32D192ED03)) mod 2^64.
+ * A sum over global indices, so the digests of the shards of an array add up
+ * to the digest of the whole array. */
+uint64_t orc_digest(const uint64_t *x, size_t count, uint64_t first_index);
 
 /* ---------------- part 3: threaded CPU baseline ---------------- */
 

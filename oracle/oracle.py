@@ -31,10 +31,18 @@ def build() -> str:
     return _SO
 
 
+def _stale() -> bool:
+    if not os.path.exists(_SO):
+        return True
+    t = os.path.getmtime(_SO)
+    srcs = [os.path.join(_HERE, f) for f in ("ref_wgsl.c", "exact.c", "baseline.c", "oracle.h")]
+    return any(os.path.exists(f) and os.path.getmtime(f) > t for f in srcs)
+
+
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_SO):
+        if _stale():
             build()
         L = ctypes.CDLL(_SO)
         u32, u64, i32 = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
@@ -69,6 +77,7 @@ def lib():
             "orc_negacyclic_convolution": (None, [_u64p, _u64p, _u64p, u32, u64]),
             "orc_seeded_value": (u64, [u64, u64, u64]),
             "orc_seeded_fill": (None, [_u64p, ctypes.c_size_t, u64, u64, u64]),
+            "orc_digest": (u64, [_u64p, ctypes.c_size_t, u64]),
             "orc_baseline_run": (ctypes.c_double,
                                  [i32, _u64p, _u64p, u32, u32, _u64p, _u64p, u32, i32]),
         }
@@ -166,6 +175,11 @@ def seeded_fill(count, seed, g0, q):
     out = np.zeros(count, dtype=np.uint64)
     lib().orc_seeded_fill(_p(out), count, seed, g0, q)
     return out
+
+
+def digest(x, first_index=0):
+    x = _arr(x)
+    return int(lib().orc_digest(_p(x), x.size, first_index))
 
 
 def ntt_prime(bits, degree, index):

@@ -337,3 +337,18 @@ def test_digest_is_order_sensitive(device):
     bc.digest(device, t2, n, out)
     device.synchronize()
     assert d1 != int(out.to_u64()[0])
+
+
+def test_digest_matches_oracle_and_adds_over_shards(device):
+    rng = np.random.default_rng(5)
+    x = rng.integers(0, 2**63, 10000, dtype=np.uint64)
+    t = upload(device, x)
+    out = _alloc(device, 1)
+    got = []
+    for first, lo, hi in ((0, 0, 10000), (0, 0, 3000), (3000, 3000, 10000)):
+        sub = upload(device, x[lo:hi])
+        bc.digest(device, sub, hi - lo, out, first_index=first)
+        device.synchronize()
+        got.append(int(out.to_u64()[0]))
+        assert got[-1] == O.digest(x[lo:hi], first)
+    assert got[0] == (got[1] + got[2]) % 2**64
