@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: N = 2^16, 48 RNS limbs (the 48 largest primes
+Workload (benchmark config 3): N = 2^16, 48 RNS limbs (the 48 largest primes
 below 2^31 with q = 1 mod 2N: the reference is exact only below 2^31),
 128 ciphertexts x 2 polynomials per GPU, layout [ct][2][limb][N] (u64), seeded
 uniform coefficients.  One step = one forward negacyclic NTT and one INTT of
@@ -37,9 +37,11 @@ CTS_PER_GPU = 128
 BYTES_PER_TRANSFORM = 16 * N        # read N u64 + write N u64 (algorithmic)
 METRIC = "negacyclic NTT limb-transforms/s at N=2^16 (fwd+inv, 48 limbs, 128 ct x 2 polys per GPU)"
 UNIT = "limb-transforms/s"
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant
-# kernel, from the ncu capture summarised in profiles/ (None until captured).
-NCU_TRAFFIC_PER_TRANSFORM = None
+# dram__bytes_read.sum + dram__bytes_write.sum of the dominant kernel per
+# limb-transform, from an ncu capture of the forward kernel at 768 transforms
+# per launch ((427.92 + 345.37) MB, `bench.py --cts 8`); DRAM traffic per
+# transform does not depend on the batch, so it is scaled to a full launch.
+NCU_TRAFFIC_PER_TRANSFORM = 1_006_895
 
 
 def peaks():
@@ -408,6 +410,53 @@ def run_e2e(args, torch, plan, lay, polys, x, X, group):
             "timing": "CUDA events around the copy/compute streams, max over ranks"}
 
 
+def run_sweep(args):
+    """Config 4 shape on one GPU: for each N, forward and inverse of a
+    [limb][poly][N] batch of about 2 GiB (u64), one JSON line per N with the
+    launch times and the fraction of the measured HBM peak (16N bytes per
+    limb-transform).  Not the headline bench line; --sweep selects it."""
+    import torch
+
+    import barracuda_b200 as bc
+
+    torch.cuda.set_device(0)
+    dev = bc.Device(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sh = stream.cuda_stream
+    hbm, peak_kind = peaks()
+    for L in range(12, 18):
+        n = 1 << L
+        limbs = 32 if L < 14 else 16
+        batch = max(1, (1 << 28) // (n * limbs))
+        qs = bc.ntt_primes(31, n, limbs)
+        plan = bc.NttPlan(dev, n, qs, [bc.negacyclic_root(q, n) for q in qs], mode=bc.NEGACYCLIC)
+        lay = bc.Layout(limb_stride=batch * n, poly_stride=n)
+        x = torch.empty(limbs * batch * n, dtype=torch.int64, device="cuda")
+        y = torch.empty_like(x)
+        plan.fill_uniform(x, batch, seed=1, layout=lay, stream=sh)
+        line = {"sweep": "config4 shape, 1 GPU", "N": n, "limbs": limbs, "batch": batch,
+                "peak_gbs": hbm, "peak_kind": peak_kind}
+        for name, fn in (("forward", plan.forward), ("inverse", plan.inverse)):
+            for _ in range(args.warmup):
+                fn(x, y, batch, layout=lay, stream=sh)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn(x, y, batch, layout=lay, stream=sh)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            gbs = limbs * batch * 16 * n / (ms / 1000.0) / 1e9
+            line[name] = {"ms": ms, "limb_transforms_per_s": limbs * batch / (ms / 1000.0),
+                          "gb_per_s": gbs, "frac": gbs / hbm}
+        print(json.dumps(line), flush=True)
+        del x, y
+        plan.close()
+    dev.close()
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -421,10 +470,14 @@ def main(argv=None):
     ap.add_argument("--e2e-steps", type=int, default=3, help="0 skips the end-to-end measurement")
     ap.add_argument("--e2e-chunks", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="per-N forward/inverse report (config 4 shape) instead of the bench line")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.sweep:
+        run_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

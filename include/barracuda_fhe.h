@@ -185,7 +185,12 @@ int bc_ntt_inverse(bc_plan *plan, const uint64_t *d_in, uint64_t *d_out, uint32_
 /* C = A * B mod q_l, coefficient-wise. */
 int bc_pointwise_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                      uint32_t batch, const bc_layout *layout, void *stream);
-/* C = INTT(NTT(A) * NTT(B)) per (limb, polynomial), one fused kernel. */
+/* C = INTT(NTT(A) * NTT(B)) per (limb, polynomial).  One fused kernel up
+ * to N = 2^14 (moduli below 2^31) or 2^13 (wider moduli); above that it
+ * transforms both operands into a temporary device buffer, multiplies and
+ * runs the inverse into C, and then needs the default layout (layout NULL
+ * or compact).  That temporary is allocated, the stream synchronized and
+ * the buffer freed on every call. */
 int bc_polymul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                uint32_t batch, const bc_layout *layout, void *stream);
 

@@ -166,7 +166,7 @@ def test_invalid_root_canary_is_structure_dependent():
 
 
 def test_prime_families_match_plan():
-    # SURVEY 8(d) examples of the two prime families
+    # largest primes q = 1 mod 2N below 2^31 (reference-exact family) and 2^60 (60-bit family)
     assert O.ntt_prime(31, 1 << 12, 0) == 2147377153
     assert O.ntt_prime(31, 1 << 14, 0) == 2147352577
     assert O.ntt_prime(31, 1 << 16, 0) == 2147352577
