@@ -1,0 +1,8 @@
+// bc_fast_w32l2_v7.cu -- instantiates the fast NTT kernels for 32-bit words, q < 2^31, schedule variant 7.
+#include "bc_kernels_fast.cuh"
+
+namespace bc {
+namespace fast {
+template int dispatch_l<Arith32<false>, 7>(uint32_t L, bool gs, bool scale, const KArgs &a, cudaStream_t s);
+}  // namespace fast
+}  // namespace bc

@@ -18,8 +18,9 @@ namespace {
 // Schedule variant of the fast kernel for a word size and N (see
 // gen_schedule.py): 4 = 16 coefficients per thread in 512-thread CTAs,
 // 5 = 32 per thread in CTAs of up to 2^14 words, 6 = 32 per thread in
-// 256-thread CTAs.  BARRACUDA_NTT_VARIANT=4|5|6 overrides the default for
-// 32-bit words where that schedule exists.
+// 256-thread CTAs, 7 = 32 per thread in 128-thread CTAs.
+// BARRACUDA_NTT_VARIANT=4|5|6|7 overrides the default for 32-bit words where
+// that schedule exists.
 int env_int(const char *name) {
     const char *e = std::getenv(name);
     return e ? std::atoi(e) : 0;
@@ -34,7 +35,8 @@ int fast_variant(Word w, uint32_t logn, bool inverse) {
     const int e = inverse ? (env_inv ? env_inv : env_all) : (env_fwd ? env_fwd : env_all);
     if (e && fast::sched_logc(L, e) >= 0) return e;
     // Measured on B200 (forward and inverse, ~2 GiB batches): 16 per thread
-    // wins for N <= 2^12, 256-thread CTAs of 32 per thread for 2^14..2^16.
+    // wins for N <= 2^12, 256-thread CTAs of 32 per thread for 2^14..2^17
+    // (clusters of 16 at 2^17); 128-thread CTAs (7) lose at 2^16.
     if (L <= 12) return 4;
     if (fast::sched_logc(L, 6) >= 0) return 6;
     return 5;
@@ -74,10 +76,12 @@ int launch_ntt_fast(Word w, bool gs, bool scale_last, const KArgs &a, cudaStream
     case Word::W32Lazy4:
         if (v == 4) return fast::dispatch_l<Arith32<true>, 4>(a.logn, gs, scale_last, a, s);
         if (v == 6) return fast::dispatch_l<Arith32<true>, 6>(a.logn, gs, scale_last, a, s);
+        if (v == 7) return fast::dispatch_l<Arith32<true>, 7>(a.logn, gs, scale_last, a, s);
         return fast::dispatch_l<Arith32<true>, 5>(a.logn, gs, scale_last, a, s);
     case Word::W32Lazy2:
         if (v == 4) return fast::dispatch_l<Arith32<false>, 4>(a.logn, gs, scale_last, a, s);
         if (v == 6) return fast::dispatch_l<Arith32<false>, 6>(a.logn, gs, scale_last, a, s);
+        if (v == 7) return fast::dispatch_l<Arith32<false>, 7>(a.logn, gs, scale_last, a, s);
         return fast::dispatch_l<Arith32<false>, 5>(a.logn, gs, scale_last, a, s);
     default: return fast::dispatch_l<Arith64, 4>(a.logn, gs, scale_last, a, s);
     }

@@ -642,6 +642,10 @@ int launch_one(const KArgs &a, cudaStream_t s) {
     if (nres == 0) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return cuda_fail(e, "k_ntt_fast shared-memory attribute");
+        if (Sh::kC > 8) {  // clusters of 16 CTAs: a non-portable size B200 supports
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return cuda_fail(e, "k_ntt_fast cluster-size attribute");
+        }
         int props = 0;
         cudaDeviceGetAttribute(&props, cudaDevAttrMultiProcessorCount, dev);
         if (Sh::kC > 1) {
@@ -695,7 +699,7 @@ int dispatch_if(bool gs, bool scale, const KArgs &a, cudaStream_t s) {
 }
 
 // Template parameter LOGE of the kernels above is the schedule variant V
-// (Sched<L, V>): 4, 5 or 6, see gen_schedule.py.
+// (Sched<L, V>): 4, 5, 6 or 7, see gen_schedule.py.
 template <class A, int V>
 int dispatch_l(uint32_t L, bool gs, bool scale, const KArgs &a, cudaStream_t s) {
     switch (L) {

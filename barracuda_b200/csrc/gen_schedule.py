@@ -49,7 +49,9 @@ OUT = os.path.join(HERE, "bc_schedule.hpp")
 # (L, variant): (loge, logc, passes [(hi, lo, extras)], rank bits phase 0, rank bits phase 1, split)
 # Variants: 4 = 16 coefficients per thread (512-thread CTAs of 2^13 words);
 # 5 = 32 per thread (CTAs of up to 2^14 words); 6 = 32 per thread in
-# 256-thread CTAs of 2^13 words (more, smaller CTAs per SM).
+# 256-thread CTAs of 2^13 words (more, smaller CTAs per SM); 7 = 32 per
+# thread in 128-thread CTAs of 2^12 words.  Clusters of 16 CTAs (L=17 V6,
+# L=16 V7) are a non-portable size that B200 allows.
 # `split` = number of passes in phase 0 (the remaining passes are phase 1).
 CONFIGS = {
     (10, 5): (5, 0, [(9, 5, []), (4, 0, [])], [], [], 2),
@@ -63,6 +65,8 @@ CONFIGS = {
     (14, 6): (5, 1, [(13, 10, [0]), (9, 5, []), (4, 0, [])], [9], [10], 1),
     (15, 6): (5, 2, [(14, 10, []), (9, 5, []), (4, 0, [])], [8, 9], [10, 11], 1),
     (16, 6): (5, 3, [(15, 13, [0, 1]), (12, 8, []), (7, 5, [0, 1]), (4, 0, [])], [5, 6, 7], [8, 9, 10], 2),
+    (17, 6): (5, 4, [(16, 13, [0]), (12, 8, []), (7, 5, [0, 1]), (4, 0, [])], [4, 5, 6, 7], [8, 9, 10, 11], 2),
+    (16, 7): (5, 4, [(15, 13, [0, 1]), (12, 8, []), (7, 5, [0, 1]), (4, 0, [])], [4, 5, 6, 7], [8, 9, 10, 11], 2),
     (10, 4): (4, 0, [(9, 8, [0, 1]), (7, 4, []), (3, 0, [])], [], [], 3),
     (11, 4): (4, 0, [(10, 8, [0]), (7, 4, []), (3, 0, [])], [], [], 3),
     (12, 4): (4, 0, [(11, 8, []), (7, 4, []), (3, 0, [])], [], [], 3),
@@ -137,6 +141,14 @@ def lane_options(L, loge, logc, passes, rank0, rank1, split, pair=True):
         cands = [(c,) for c in itertools.combinations(sorted(thread_bits[i]), 5)]
         units.append(((i,), cands))
         i += 1
+    # The passes on either side of the phase change store into the other
+    # phase's layout (CT: pass split-1 into phase 1, GS: pass split into
+    # phase 0), so their lanes must be local bits there too.
+    if logc:
+        avoid = {split - 1: set(rank1), split: set(rank0)}
+        units = [(idx, [c for c in cands
+                        if all(not (set(ln) & avoid.get(j, set())) for j, ln in zip(idx, c))])
+                 for idx, cands in units]
     return units, thread_bits
 
 
