@@ -56,6 +56,10 @@ int launch_ntt_fast(Word w, bool gs, bool scale_last, const KArgs &a, cudaStream
 // which stores each stage's twiddles transposed per pass (pair = 2 for
 // 8-byte entries, 1 for 16-byte entries).
 int fast_variant_for(Word w, uint32_t logn, bool inverse);
+// Fused negacyclic polymul on the fast schedules: a.in = A, a.in2 = NTT(B)
+// in natural order (may alias a.out), a.out = C, a.tw / a.tw2 = the fast
+// forward / inverse tables.  Needs the same variant in both directions.
+int launch_polymul_fast(Word w, const KArgs &a, cudaStream_t s);
 uint64_t fast_table_index(uint32_t L, int V, uint64_t knat, int pair);
 
 // Multi-pass global-memory path for any N (one launch per stage) through a

@@ -12,6 +12,8 @@ namespace bc {
 namespace fast {
 template <class A, int LOGE>
 int dispatch_l(uint32_t L, bool gs, bool scale, const KArgs &a, cudaStream_t s);
+template <class A, int LOGE>
+int dispatch_polymul_l(uint32_t L, const KArgs &a, cudaStream_t s);
 }  // namespace fast
 
 namespace {
@@ -84,6 +86,25 @@ int launch_ntt_fast(Word w, bool gs, bool scale_last, const KArgs &a, cudaStream
         if (v == 7) return fast::dispatch_l<Arith32<false>, 7>(a.logn, gs, scale_last, a, s);
         return fast::dispatch_l<Arith32<false>, 5>(a.logn, gs, scale_last, a, s);
     default: return fast::dispatch_l<Arith64, 4>(a.logn, gs, scale_last, a, s);
+    }
+}
+
+int launch_polymul_fast(Word w, const KArgs &a, cudaStream_t s) {
+    const int v = fast_variant(w, a.logn, false);
+    if (v != fast_variant(w, a.logn, true))
+        return fail(BC_ERR_INTERNAL, "fused polymul needs one schedule for both directions");
+    switch (w) {
+    case Word::W32Lazy4:
+        if (v == 4) return fast::dispatch_polymul_l<Arith32<true>, 4>(a.logn, a, s);
+        if (v == 6) return fast::dispatch_polymul_l<Arith32<true>, 6>(a.logn, a, s);
+        if (v == 7) return fast::dispatch_polymul_l<Arith32<true>, 7>(a.logn, a, s);
+        return fast::dispatch_polymul_l<Arith32<true>, 5>(a.logn, a, s);
+    case Word::W32Lazy2:
+        if (v == 4) return fast::dispatch_polymul_l<Arith32<false>, 4>(a.logn, a, s);
+        if (v == 6) return fast::dispatch_polymul_l<Arith32<false>, 6>(a.logn, a, s);
+        if (v == 7) return fast::dispatch_polymul_l<Arith32<false>, 7>(a.logn, a, s);
+        return fast::dispatch_polymul_l<Arith32<false>, 5>(a.logn, a, s);
+    default: return fast::dispatch_polymul_l<Arith64, 4>(a.logn, a, s);
     }
 }
 

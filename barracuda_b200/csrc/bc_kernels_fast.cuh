@@ -442,6 +442,41 @@ struct Coop {
         }
     }
 
+    // Multiplies the CTA's share of the working array, coefficient-wise mod
+    // q, by `src` (canonical residues in this stage's order): the pointwise
+    // product of a fused polynomial multiplication.
+    __device__ __forceinline__ static void mul(W *smem, const uint64_t *src, uint32_t rank,
+                                               const LimbConst &lc) {
+        const uint32_t tid = threadIdx.x;
+        const uint32_t kr = NAT ? rank_pos<S>(rank, PHASE) : (__brev(rank_pos<S>(rank, PHASE)) >> (32 - L));
+        const uint32_t kt = natural_of<S, L>(2 * tid, PHASE, NAT) + kr;
+        const uint32_t at = smem_of_natural<S, L>(natural_of<S, L>(2 * tid, PHASE, NAT), PHASE, NAT);
+        constexpr uint32_t a1 = smem_of_natural<S, L>(natural_of<S, L>(1, PHASE, NAT), PHASE, NAT);
+        constexpr int kBatch = A::kBits == 32 ? 8 : 4;
+#pragma unroll
+        for (int j0 = 0; j0 < kIters; j0 += kBatch) {
+            ulonglong2 x[kBatch];
+#pragma unroll
+            for (int j = 0; j < kBatch && j0 + j < kIters; ++j)
+                x[j] = __ldcs(reinterpret_cast<const ulonglong2 *>(
+                    src + kt + natural_of<S, L>(2 * (j0 + j) * T, PHASE, NAT)));
+#pragma unroll
+            for (int j = 0; j < kBatch && j0 + j < kIters; ++j) {
+                const uint32_t a0 = at + smem_of_natural<S, L>(natural_of<S, L>(2 * (j0 + j) * T, PHASE, NAT),
+                                                               PHASE, NAT);
+                smem[a0] = mulmod_lc(smem[a0], static_cast<W>(x[j].x), lc);
+                smem[a0 + a1] = mulmod_lc(smem[a0 + a1], static_cast<W>(x[j].y), lc);
+            }
+        }
+    }
+
+    __device__ __forceinline__ static W mulmod_lc(W x, W y, const LimbConst &lc) {
+        if constexpr (A::kBits == 32)
+            return A::mulmod(x, y, static_cast<W>(lc.q), lc.barrett);
+        else
+            return A::mulmod(x, y, lc.q, lc.barrett, lc.bk);
+    }
+
     __device__ __forceinline__ static void store(const W *smem, uint64_t *dst, uint32_t rank,
                                                  const LimbConst &lc) {
         const uint32_t tid = threadIdx.x;
@@ -670,6 +705,86 @@ int launch_one(const KArgs &a, cudaStream_t s) {
     return BC_OK;
 }
 
+// Fused negacyclic polynomial product, one cluster per (limb, pair):
+// C = INTT(NTT(A) * B^), where B^ = NTT(B) in natural order (a forward launch
+// writes it, possibly into C itself).  The forward passes, the pointwise
+// product and the inverse passes all run on the working array, so HBM sees
+// A and B^ read once and C written once (24N bytes per pair).  B^ may alias
+// C: every CTA reads its share of B^ before the cluster barrier of the
+// inverse's phase change, and writes C only after it.
+template <class A, int L, int LOGE>
+__global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, false>::kMinBlocks))
+    k_polymul_fast(KArgs a) {
+    using W = typename A::W;
+    using Sh = Shape<L, LOGE>;
+    using S = Sched<L, LOGE>;
+    using Fwd = Step<A, L, LOGE, false, false, 0>;
+    using Inv = Step<A, L, LOGE, true, true, 0>;
+    constexpr int ph_first = S::pass(0).phase, ph_last = S::pass(S::kPasses - 1).phase;
+    using In = Coop<A, S, L, Sh::kT, Sh::kLocal, ph_first, true>;   // A, natural order
+    using Mid = Coop<A, S, L, Sh::kT, Sh::kLocal, ph_last, false>;  // B^, NTT-domain order
+    using Out = Coop<A, S, L, Sh::kT, Sh::kLocal, ph_first, true>;  // C, natural order
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    W *work = reinterpret_cast<W *>(smem_raw);
+    const uint32_t rank = Sh::kC > 1 ? cluster_rank() : 0u;
+    const uint64_t cl = blockIdx.x / Sh::kC;
+    const uint64_t limb = cl / a.batch, poly = cl % a.batch;
+    const int64_t base = static_cast<int64_t>(limb) * a.limb_stride + static_cast<int64_t>(poly) * a.poly_stride;
+    const LimbConst &lc = a.limbs[limb];
+    const typename A::Tw *tw = reinterpret_cast<const typename A::Tw *>(a.tw) + (limb << L);
+    const typename A::Tw *tw2 = reinterpret_cast<const typename A::Tw *>(a.tw2) + (limb << L);
+    uint32_t bad = 0;
+    In::load(work, a.in + base, rank, lc, bad);
+    typename Fwd::Ring ring_f;
+    Fwd::prefetch(ring_f, tw, rank);
+    __syncthreads();
+    Fwd::run(work, tw, lc, rank, ring_f);  // ends with the working array complete
+    Mid::mul(work, a.in2 + base, rank, lc);
+    typename Inv::Ring ring_i;
+    Inv::prefetch(ring_i, tw2, rank);
+    __syncthreads();
+    Inv::run(work, tw2, lc, rank, ring_i);
+    Out::store(work, a.out + base, rank, lc);
+    if constexpr (A::kBits == 32) {
+        if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) atomicOr(a.status, kStatusInputRange);
+    }
+}
+
+template <class A, int L, int LOGE>
+int launch_polymul_one(const KArgs &a, cudaStream_t s) {
+    using Sh = Shape<L, LOGE>;
+    auto kern = k_polymul_fast<A, L, LOGE>;
+    const size_t smem = Smem<A, L, LOGE, false>::kBytes;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return cuda_fail(e, "k_polymul_fast shared-memory attribute");
+        if (Sh::kC > 8) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return cuda_fail(e, "k_polymul_fast cluster-size attribute");
+        }
+        if (dev < 64) attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(Sh::kT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = Sh::kC;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = Sh::kC > 1 ? 1 : 0;
+    const uint64_t polys = static_cast<uint64_t>(a.batch) * a.n_limbs;
+    cfg.gridDim = dim3(static_cast<unsigned>(polys * Sh::kC));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+    if (e != cudaSuccess) return cuda_fail(e, "k_polymul_fast launch");
+    return BC_OK;
+}
+
 // Persistent prefetching launches are not used by default: with their
 // staging buffers only two 512-thread CTAs fit an SM, and measured on
 // B200 that loses more to barrier and shared-memory-queue stalls than the
@@ -696,6 +811,29 @@ template <class A, int V, int L>
 int dispatch_if(bool gs, bool scale, const KArgs &a, cudaStream_t s) {
     if constexpr (sched_logc(L, V) >= 0) return dispatch_dir<A, V, L>(gs, scale, a, s);
     return fail(BC_ERR_INTERNAL, format("no fast schedule for log2 N = %d, variant %d", L, V));
+}
+
+template <class A, int V, int L>
+int polymul_if(const KArgs &a, cudaStream_t s) {
+    if constexpr (sched_logc(L, V) >= 0) return launch_polymul_one<A, L, V>(a, s);
+    return fail(BC_ERR_INTERNAL, format("no fast schedule for log2 N = %d, variant %d", L, V));
+}
+
+// Fused polymul for the fast sizes (see k_polymul_fast).
+template <class A, int V>
+int dispatch_polymul_l(uint32_t L, const KArgs &a, cudaStream_t s) {
+    switch (L) {
+    case 10: return polymul_if<A, V, 10>(a, s);
+    case 11: return polymul_if<A, V, 11>(a, s);
+    case 12: return polymul_if<A, V, 12>(a, s);
+    case 13: return polymul_if<A, V, 13>(a, s);
+    case 14: return polymul_if<A, V, 14>(a, s);
+    case 15: return polymul_if<A, V, 15>(a, s);
+    case 16: return polymul_if<A, V, 16>(a, s);
+    case 17: return polymul_if<A, V, 17>(a, s);
+    default: break;
+    }
+    return fail(BC_ERR_INTERNAL, format("no fast schedule for log2 N = %u", L));
 }
 
 // Template parameter LOGE of the kernels above is the schedule variant V

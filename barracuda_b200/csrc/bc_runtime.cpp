@@ -342,18 +342,64 @@ int run_pointwise(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t *c
     return launch_pointwise(p->word, a, s);
 }
 
-int run_polymul(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t *c, uint32_t batch,
-                const bc_layout *layout, cudaStream_t s) {
+namespace {
+
+// How run_polymul computes a product (see there).
+enum class PolymulPath { Smem, Fast, Unfused };
+
+PolymulPath polymul_path(const bc_plan *p, const KArgs &a) {
+    if (p->logn >= 1 && p->logn <= polymul_smem_max_logn(p->word)) return PolymulPath::Smem;
+    const auto aligned = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const bool all_alias = a.in == a.out && a.in2 == a.out;
+    if (p->mode == BC_NTT_NEGACYCLIC && p->kind == KernelKind::Cluster && fast_layout_ok(a) &&
+        aligned(a.in2) && !all_alias &&
+        fast_variant_for(p->word, p->logn, false) == fast_variant_for(p->word, p->logn, true))
+        return PolymulPath::Fast;
+    return PolymulPath::Unfused;
+}
+
+}  // namespace
+
+bool polymul_allocates(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t *c, uint32_t batch,
+                       const bc_layout *layout) {
+    KArgs a;
+    if (make_args(p, a_, b, c, batch, layout, &a) != BC_OK) return false;  // run_polymul fails first
+    return polymul_path(p, a) == PolymulPath::Unfused;
+}
+
+namespace {
+
+int run_polymul_impl(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t *c, uint32_t batch,
+                     const bc_layout *layout, cudaStream_t s) {
     KArgs a;
     int st = make_args(p, a_, b, c, batch, layout, &a);
     if (st) return st;
     if (!b) return fail(BC_ERR_INVALID_INPUT, "device pointers must not be NULL");
     if ((st = use_device(p->ctx))) return st;
     const bool cyclic = p->mode == BC_NTT_CYCLIC;
-    if (p->logn >= 1 && p->logn <= polymul_smem_max_logn(p->word)) {
+    switch (polymul_path(p, a)) {
+    case PolymulPath::Smem:
         a.tw = p->d_tw_fwd;
         a.tw2 = p->d_tw_inv;
         return launch_polymul_smem(p->word, cyclic, a, s);
+    case PolymulPath::Fast: {
+        // Negacyclic, fast schedules: C <- NTT(y), then one fused kernel
+        // C <- INTT(NTT(x) * C).  The product commutes, so when A aliases C
+        // the roles swap and A's transform is the one written into C.
+        const uint64_t *x = a_, *y = b;
+        if (x == c) std::swap(x, y);
+        KArgs f = a;
+        f.in = y;
+        f.in2 = nullptr;
+        f.tw = p->d_tw_fwd_fast;
+        if ((st = launch_ntt_fast(p->word, false, false, f, s))) return st;
+        a.in = x;
+        a.in2 = c;
+        a.tw = p->d_tw_fwd_fast;
+        a.tw2 = p->d_tw_inv_fast;
+        return launch_polymul_fast(p->word, a, s);
+    }
+    default: break;
     }
     // Unfused fallback above the fused size: forward both operands into a
     // temporary compact buffer, multiply, inverse into the caller's layout.
@@ -373,6 +419,13 @@ int run_polymul(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t *c, 
     cudaStreamSynchronize(s);
     cudaFree(tmp);
     return r;
+}
+
+}  // namespace
+
+int run_polymul(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t *c, uint32_t batch,
+                const bc_layout *layout, cudaStream_t s) {
+    return run_polymul_impl(p, a_, b, c, batch, layout, s);
 }
 
 int cached_plan(bc_ctx *ctx, uint32_t degree, uint64_t modulus, uint64_t root, uint64_t inv_root,

@@ -79,5 +79,9 @@ int run_pointwise(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c,
                   uint32_t batch, const bc_layout *layout, cudaStream_t s);
 int run_polymul(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c,
                 uint32_t batch, const bc_layout *layout, cudaStream_t s);
+// Whether run_polymul would take its unfused path, which allocates, syncs
+// and frees a temporary buffer (false when the arguments are invalid).
+bool polymul_allocates(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c,
+                       uint32_t batch, const bc_layout *layout);
 
 }  // namespace bc

@@ -1,7 +1,8 @@
 // bc_static_scratch.cu -- bc_polymul_static_scratch: the NTT-based
 // polynomial product without any device allocation.
 //
-// Above the fused size bc_polymul runs forward(A) and forward(B) into a
+// On its unfused path (cyclic plans above the fused size, layouts the fused
+// kernels cannot take) bc_polymul runs forward(A) and forward(B) into a
 // temporary device buffer, multiplies, and runs the inverse; it allocates
 // that buffer with cudaMalloc, synchronizes the stream and frees it on every
 // call.  Some callers cannot do that during the call:
@@ -105,9 +106,8 @@ extern "C" int bc_polymul_static_scratch(bc_plan *p, const uint64_t *a, const ui
                                          void *stream) {
     if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : p->ctx->stream;
-    // Fused sizes use no scratch: the product is bc_polymul's own kernel.
-    if (p->logn >= 1 && p->logn <= polymul_smem_max_logn(p->word))
-        return run_polymul(p, a, b, c, batch, layout, s);
+    // Where bc_polymul needs no temporary (its fused kernels), it is the product.
+    if (!polymul_allocates(p, a, b, c, batch, layout)) return run_polymul(p, a, b, c, batch, layout, s);
     if (batch == 0) return fail(BC_ERR_INVALID_INPUT, "batch must be at least 1");
     if (!a || !b || !c) return fail(BC_ERR_INVALID_INPUT, "device pointers must not be NULL");
     if (layout && (layout->poly_stride != p->degree ||

@@ -367,7 +367,7 @@ def run_e2e(args, torch, plan, lay, polys, x, X, group):
     host.copy_(x, non_blocking=False)
     chunks = max(1, args.e2e_chunks)
     cts = polys // 2
-    streams = [torch.cuda.Stream() for _ in range(2)]
+    streams = [torch.cuda.Stream() for _ in range(max(1, args.e2e_streams))]
     per = [(c * cts) // chunks for c in range(chunks + 1)]
     elem_per_ct = 2 * LIMBS * N
 
@@ -376,7 +376,7 @@ def run_e2e(args, torch, plan, lay, polys, x, X, group):
         for s in streams:
             s.wait_stream(cur)
         for c in range(chunks):
-            s = streams[c % 2]
+            s = streams[c % len(streams)]
             lo, hi = per[c] * elem_per_ct, per[c + 1] * elem_per_ct
             if hi == lo:
                 continue
@@ -406,7 +406,7 @@ def run_e2e(args, torch, plan, lay, polys, x, X, group):
     units = 2 * limb_polys * steps
     return {"value": units / secs, "unit": UNIT,
             "h2d_bytes_per_step": limb_polys * N * 8, "d2h_bytes_per_step": limb_polys * N * 8,
-            "steps": steps, "chunks": chunks,
+            "steps": steps, "chunks": chunks, "streams": len(streams),
             "timing": "CUDA events around the copy/compute streams, max over ranks"}
 
 
@@ -468,7 +468,8 @@ def main(argv=None):
     ap.add_argument("--cts", type=int, default=CTS_PER_GPU,
                     help="ciphertexts per GPU (weak scaling); smaller values make the profiling case")
     ap.add_argument("--e2e-steps", type=int, default=3, help="0 skips the end-to-end measurement")
-    ap.add_argument("--e2e-chunks", type=int, default=8)
+    ap.add_argument("--e2e-chunks", type=int, default=32)
+    ap.add_argument("--e2e-streams", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="per-N forward/inverse report (config 4 shape) instead of the bench line")

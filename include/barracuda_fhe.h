@@ -185,25 +185,31 @@ int bc_ntt_inverse(bc_plan *plan, const uint64_t *d_in, uint64_t *d_out, uint32_
 /* C = A * B mod q_l, coefficient-wise. */
 int bc_pointwise_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                      uint32_t batch, const bc_layout *layout, void *stream);
-/* C = INTT(NTT(A) * NTT(B)) per (limb, polynomial).  One fused kernel up
- * to N = 2^14 (moduli below 2^31) or 2^13 (wider moduli); above that it
- * transforms both operands into a temporary device buffer, multiplies and
- * runs the inverse into C, and then needs the default layout (layout NULL
- * or compact).  That temporary is allocated, the stream synchronized and
- * the buffer freed on every call. */
+/* C = INTT(NTT(A) * NTT(B)) per (limb, polynomial).  Up to N = 2^14
+ * (moduli below 2^31) or 2^13 (wider moduli): one fused kernel.  Above that,
+ * negacyclic plans on the cluster kernels (16-byte aligned operands, even
+ * strides, not A == B == C) run two launches: NTT(B) into C, then one fused
+ * kernel C = INTT(NTT(A) * C); nothing is allocated.  Every other case
+ * (cyclic plans above the fused size, other layouts) transforms both
+ * operands into a temporary device buffer, multiplies and runs the inverse
+ * into C, needing the default layout (layout NULL or compact); that
+ * temporary is allocated, the stream synchronized and the buffer freed on
+ * every call. */
 int bc_polymul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                uint32_t batch, const bc_layout *layout, void *stream);
 
-/* Largest batch * n_limbs * N that bc_polymul_static_scratch accepts above
- * the fused size (2^21 coefficients per operand; the buffer is 32 MiB). */
+/* Largest batch * n_limbs * N that bc_polymul_static_scratch accepts where
+ * bc_polymul would allocate (2^21 coefficients per operand; the buffer is
+ * 32 MiB). */
 #define BC_POLYMUL_STATIC_MAX_COEFFS (1u << 21)
 
 /* bc_polymul that never allocates device memory.  No counterpart in the
  * reference: FheFastPolyMul::execute (ops/fhe_fast_poly_mul.rs:122)
  * allocates its intermediates and output on every call.
  *
- * Who needs it: above the fused size (N > 2^14 for moduli below 2^31,
- * N > 2^13 otherwise) bc_polymul allocates a temporary device buffer,
+ * Who needs it: on its unfused path (see bc_polymul: cyclic plans above
+ * N = 2^14 for moduli below 2^31 or 2^13 otherwise, layouts the fused
+ * kernels cannot take) bc_polymul allocates a temporary device buffer,
  * synchronizes the stream and frees the buffer on every call.  A caller
  * cannot afford that when the device memory is already reserved by another
  * allocator (a framework's caching pool leaves cudaMalloc nothing to hand
@@ -213,11 +219,11 @@ int bc_polymul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t
  * device memory instead.  It computes the same result as bc_polymul and
  * neither allocates nor synchronizes.
  *
- * Limits: above the fused size, batch * n_limbs * N must not exceed
- * BC_POLYMUL_STATIC_MAX_COEFFS, and `layout` must be NULL or the default
- * compact layout.  Larger or strided calls fail with BC_ERR_INVALID_INPUT /
- * BC_ERR_UNSUPPORTED before any work is queued.  At fused sizes it is
- * bc_polymul and has no size limit.
+ * Limits: where bc_polymul would allocate, batch * n_limbs * N must not
+ * exceed BC_POLYMUL_STATIC_MAX_COEFFS, and `layout` must be NULL or the
+ * default compact layout.  Larger or strided calls fail with
+ * BC_ERR_INVALID_INPUT / BC_ERR_UNSUPPORTED before any work is queued.
+ * Where bc_polymul's fused kernels apply it is bc_polymul, with no limit.
  *
  * Sharing: every call on a GPU uses the same buffer.  Calls on one stream
  * are ordered and safe.  Calls that overlap in time race on the buffer and

@@ -272,7 +272,7 @@ def test_plan_strided_ciphertext_layout_and_in_place(device):
     assert (buf.to_u64() == x).all()
 
 
-@pytest.mark.parametrize("logn,bits", [(12, 31), (14, 31), (15, 31), (13, 60)])
+@pytest.mark.parametrize("logn,bits", [(12, 31), (14, 31), (15, 31), (16, 31), (17, 31), (13, 60), (15, 60)])
 @pytest.mark.parametrize("mode", [bc.NEGACYCLIC, bc.CYCLIC])
 def test_plan_polymul_matches_chain(device, logn, bits, mode):
     n, limbs, batch = 1 << logn, 2, 2
@@ -323,6 +323,37 @@ def test_plan_pointwise(device):
     for l in range(limbs):
         sl = slice(l * batch * n, (l + 1) * batch * n)
         assert (C[sl] == O.ref_pointwise(A[sl], B[sl], batch * n, qs[l])).all()
+
+
+@pytest.mark.parametrize("bits", [31, 60])
+def test_polymul_aliasing(device, bits):
+    """C may alias A, B or both (squaring in place); results as with separate buffers."""
+    n, limbs, batch = 1 << 15, 2, 2
+    plan, qs, roots = _plan(device, n, limbs, bits, bc.NEGACYCLIC)
+    total = limbs * batch * n
+    a, b, c, ref, sq = (_alloc(device, total) for _ in range(5))
+    plan.fill_uniform(a, batch, seed=3)
+    plan.fill_uniform(b, batch, seed=4)
+    plan.polymul(a, b, ref, batch)
+    plan.polymul(a, a, sq, batch)
+    device.synchronize()
+    A, B, want, want_sq = a.to_u64(), b.to_u64(), ref.to_u64(), sq.to_u64()
+
+    def put(t, x):
+        N.check(N.lib().bc_buf_h2d(device.handle, t.ptr, x.ctypes.data, x.nbytes))
+
+    put(c, A)
+    plan.polymul(c, b, c, batch)          # C aliases A
+    device.synchronize()
+    assert (c.to_u64() == want).all()
+    put(c, B)
+    plan.polymul(a, c, c, batch)          # C aliases B
+    device.synchronize()
+    assert (c.to_u64() == want).all()
+    put(c, A)
+    plan.polymul(c, c, c, batch)          # A == B == C
+    device.synchronize()
+    assert (c.to_u64() == want_sq).all()
 
 
 def test_digest_is_order_sensitive(device):

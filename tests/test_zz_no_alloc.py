@@ -27,12 +27,13 @@ def _buf(device, count):
 
 
 @pytest.mark.parametrize("logn,limbs,batch,bits,mode", [
-    (15, 2, 8, 31, bc.NEGACYCLIC),   # above the fused size, fast kernels
-    (15, 2, 4, 31, bc.CYCLIC),
-    (14, 2, 4, 60, bc.NEGACYCLIC),   # 64-bit words above their fused size
+    (15, 2, 8, 31, bc.NEGACYCLIC),   # fused cluster kernels, no scratch
+    (15, 2, 4, 31, bc.CYCLIC),       # unfused path in the static buffer
+    (14, 2, 4, 60, bc.NEGACYCLIC),   # 64-bit words, fused cluster kernels
     (17, 1, 2, 31, bc.NEGACYCLIC),
     (17, 1, 2, 60, bc.NEGACYCLIC),   # multi-pass global path in the static buffer
     (12, 2, 2, 31, bc.NEGACYCLIC),   # fused size: no scratch at all
+    (14, 2, 4, 60, bc.CYCLIC),       # unfused path, 64-bit words
 ])
 def test_static_scratch_polymul_matches_polymul(device, logn, limbs, batch, bits, mode):
     n = 1 << logn
@@ -53,9 +54,10 @@ def test_static_scratch_polymul_matches_polymul(device, logn, limbs, batch, bits
 
 
 def test_static_scratch_polymul_rejects_oversize_and_strided(device):
+    # cyclic above the fused size: the case where bc_polymul would allocate
     n, limbs = 1 << 15, 4
     batch = MAX_COEFFS // (limbs * n) + 1
-    plan = _plan(device, n, limbs, 31, bc.NEGACYCLIC)
+    plan = _plan(device, n, limbs, 31, bc.CYCLIC)
     total = limbs * batch * n
     a, b, c = _buf(device, total), _buf(device, total), _buf(device, total)
     lib = N.lib()
