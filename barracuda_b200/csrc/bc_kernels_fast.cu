@@ -63,7 +63,7 @@ uint64_t fast_table_index(uint32_t L, int V, uint64_t knat, int pair) {
 }
 
 bool fast_supported(Word w, uint32_t logn) {
-    if (w == Word::W64) return logn >= 10 && logn <= 16;
+    if (w == Word::W64) return logn >= 10 && logn <= 17;
     return logn >= 10 && logn <= 17;
 }
 

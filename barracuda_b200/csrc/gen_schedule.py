@@ -74,6 +74,8 @@ CONFIGS = {
     (14, 4): (4, 1, [(13, 12, [0, 1]), (11, 8, []), (7, 4, []), (3, 0, [])], [6], [8], 2),
     (15, 4): (4, 2, [(14, 12, [0]), (11, 8, []), (7, 4, []), (3, 0, [])], [5, 6], [8, 9], 2),
     (16, 4): (4, 3, [(15, 12, []), (11, 8, []), (7, 4, []), (3, 0, [])], [5, 6, 7], [8, 9, 10], 2),
+    (17, 4): (4, 4, [(16, 16, [0, 1, 2]), (15, 12, []), (11, 8, []), (7, 4, []), (3, 0, [])],
+              [4, 5, 6, 7], [8, 9, 10, 11], 3),
 }
 
 
