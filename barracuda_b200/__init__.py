@@ -9,7 +9,8 @@ no CPU fallback: without the library every call raises.
 from ._native import BarracudaError, NativeLibraryMissing, LIB_PATH  # noqa: F401
 from .ops import (  # noqa: F401
     Device, FheTensor, create_fhe_poly_tensor, read_poly_from_tensor, compute_primitive_root,
-    compute_inverse_root, FheNtt, FheIntt, FhePointwiseMul, FheFastPolyMul,
+    compute_inverse_root, FheNtt, FheIntt, FhePointwiseMul, FheFastPolyMul, FhePolyAdd, FhePolySub,
+    FhePolyMul,
 )
 from .plan import (  # noqa: F401
     NttPlan, Layout, CYCLIC, NEGACYCLIC, ntt_prime, ntt_primes, negacyclic_root, partition, digest,

@@ -102,12 +102,21 @@ SIGNATURES = {
     "bc_fhe_pointwise_mul_check": (_i32, [_sz, _sz, _u32, _u64]),
     "bc_fhe_pointwise_mul": (_i32, [_vp, _vp, _sz, _vp, _sz, _u32, _u64, _vp]),
     "bc_fhe_fast_poly_mul_check": (_i32, [_sz, _sz, _u32, _u64, _u64]),
+    "bc_fhe_poly_add_check": (_i32, [_sz, _sz, _u32, _u64]),
+    "bc_fhe_poly_add": (_i32, [_vp, _vp, _sz, _vp, _sz, _u32, _u64, _vp]),
+    "bc_fhe_poly_sub_check": (_i32, [_sz, _sz, _u32, _u64]),
+    "bc_fhe_poly_sub": (_i32, [_vp, _vp, _sz, _vp, _sz, _u32, _u64, _vp]),
+    "bc_fhe_poly_mul_check": (_i32, [_sz, _sz, _u32, _u64]),
+    "bc_fhe_poly_mul": (_i32, [_vp, _vp, _sz, _vp, _sz, _u32, _u64, _vp]),
     "bc_fhe_fast_poly_mul": (_i32, [_vp, _vp, _sz, _vp, _sz, _u32, _u64, _u64, _vp]),
     "bc_plan_create": (_i32, [_vp, _u32, _u32, _u64p, _u64p, _u64p, _i32, ctypes.POINTER(_vp)]),
     "bc_plan_destroy": (_i32, [_vp]),
     "bc_plan_info_get": (_i32, [_vp, ctypes.POINTER(bc_plan_info)]),
     "bc_ntt_forward": (_i32, [_vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_ntt_inverse": (_i32, [_vp, _vp, _vp, _u32, _lay, _vp]),
+    "bc_poly_add": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
+    "bc_poly_sub": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
+    "bc_poly_mul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_pointwise_mul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_polymul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_polymul_static_scratch": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),

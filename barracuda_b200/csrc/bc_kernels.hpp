@@ -80,6 +80,23 @@ uint32_t polymul_smem_max_logn(Word w);
 // Multiplies every coefficient by N^-1 (degree-1 inverse transform).
 int launch_scale(Word w, const KArgs &a, cudaStream_t s);
 
+// Coefficient-wise ops (FhePolyAdd / FhePolySub / FhePolyMul) on u64 words
+// of any value, with one modulus per limb.
+struct CoeffConst {
+    uint64_t q;
+    uint64_t m;   // floor((2^64 - 1) / q): quotient estimate for any u64
+    uint64_t mu;  // floor(2^(2k) / q), k = bit length of q (products for 2^32 <= q < 2^62)
+    uint32_t k;
+    uint32_t pad;
+};
+CoeffConst coeff_const(uint64_t q);  // q != 0
+enum CoeffOp : int { kCoeffAdd = 0, kCoeffSub = 1, kCoeffMul = 2 };
+// C = A op B for a.batch polynomials of n coefficients per limb (layout
+// strides in `a`); `consts` holds one CoeffConst per limb on the device, or
+// is NULL and `single` serves every limb.
+int launch_coeff_op(int op, const KArgs &a, uint64_t n, const CoeffConst *consts,
+                    const CoeffConst &single, cudaStream_t s);
+
 int launch_fill_uniform(const KArgs &a, uint64_t seed, uint64_t first_poly,
                         uint64_t total_polys, cudaStream_t s);
 int launch_digest(const uint64_t *in, size_t count, uint64_t first, uint64_t *out, cudaStream_t s);

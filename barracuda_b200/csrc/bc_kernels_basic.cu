@@ -289,6 +289,59 @@ __global__ void __launch_bounds__(512) k_polymul_smem(KArgs a) {
     }
 }
 
+// ---- coefficient-wise ops ----
+// Semantics (crates/barracuda/src/ops/, for any u64 inputs):
+//   add: the wrapping 64-bit sum minus q at most twice (fhe_poly_add.wgsl
+//        u64_add + mod_reduce), which is (a + b) mod q for a, b < q;
+//   sub: a - b if a >= b, else (q - b) + a, wrapping (fhe_poly_sub.wgsl
+//        modular_sub), which is (a - b) mod q for a, b < q;
+//   mul: exact (a * b) mod q.  The reference's fhe_poly_mul.wgsl is exact
+//        only while its product stays below 1001 q (a bounded subtraction
+//        loop) and its 32x32 helper does not overflow; outside that range
+//        this path keeps the exact residue.
+
+// x mod q for any u64 x: the estimate floor(x m / 2^64) is at most two
+// below floor(x / q).
+__device__ __forceinline__ uint64_t reduce_any(uint64_t x, const CoeffConst &c) {
+    uint64_t r = x - __umul64hi(x, c.m) * c.q;
+    if (r >= c.q) r -= c.q;
+    if (r >= c.q) r -= c.q;
+    return r;
+}
+
+__device__ __forceinline__ uint64_t mulmod_any(uint64_t a, uint64_t b, const CoeffConst &c) {
+    const uint64_t x = reduce_any(a, c), y = reduce_any(b, c);
+    if (c.q <= 0xFFFFFFFFull) return reduce_any(x * y, c);  // x * y < 2^64
+    if (c.k <= 62) return Arith64::mulmod(x, y, c.q, c.mu, c.k);
+    const unsigned __int128 p = static_cast<unsigned __int128>(x) * y;  // q >= 2^62: rare
+    return static_cast<uint64_t>(p % c.q);
+}
+
+template <int OP>
+__global__ void k_coeff(KArgs a, uint64_t n, const CoeffConst *consts, CoeffConst single) {
+    const uint64_t polys = static_cast<uint64_t>(a.batch) * a.n_limbs;
+    for (uint64_t pl = blockIdx.y; pl < polys; pl += gridDim.y) {
+        const uint64_t limb = pl / a.batch, poly = pl % a.batch;
+        const CoeffConst c = consts ? consts[limb] : single;
+        const int64_t base = static_cast<int64_t>(limb) * a.limb_stride + static_cast<int64_t>(poly) * a.poly_stride;
+        for (uint64_t j = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; j < n;
+             j += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+            const uint64_t x = __ldcs(a.in + base + j), y = __ldcs(a.in2 + base + j);
+            uint64_t r;
+            if constexpr (OP == kCoeffAdd) {
+                r = x + y;
+                if (r >= c.q) r -= c.q;
+                if (r >= c.q) r -= c.q;
+            } else if constexpr (OP == kCoeffSub) {
+                r = x >= y ? x - y : (c.q - y) + x;
+            } else {
+                r = mulmod_any(x, y, c);
+            }
+            __stcs(a.out + base + j, r);
+        }
+    }
+}
+
 // ---- synthetic inputs and digests ----
 
 __device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
@@ -469,6 +522,33 @@ int launch_fill_uniform(const KArgs &a, uint64_t seed, uint64_t first_poly, uint
     const uint64_t total = (1ull << a.logn) * a.batch * a.n_limbs;
     k_fill_uniform<<<grid_for(total, 256), 256, 0, s>>>(a, seed, first_poly, total_polys);
     return check_launch("k_fill_uniform");
+}
+
+CoeffConst coeff_const(uint64_t q) {
+    CoeffConst c = {};
+    c.q = q;
+    c.m = ~0ull / q;
+    c.k = 64 - static_cast<uint32_t>(__builtin_clzll(q));
+    if (c.k > 32 && c.k <= 62)
+        c.mu = static_cast<uint64_t>((static_cast<unsigned __int128>(1) << (2 * c.k)) / q);
+    return c;
+}
+
+int launch_coeff_op(int op, const KArgs &a, uint64_t n, const CoeffConst *consts,
+                    const CoeffConst &single, cudaStream_t s) {
+    const uint64_t polys = static_cast<uint64_t>(a.batch) * a.n_limbs;
+    if (n == 0 || polys == 0) return BC_OK;
+    const unsigned T = 256;
+    uint64_t bx = (n + T - 1) / T;
+    if (bx > 64) bx = 64;
+    const dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(polys < 65535 ? polys : 65535));
+    switch (op) {
+    case kCoeffAdd: k_coeff<kCoeffAdd><<<grid, T, 0, s>>>(a, n, consts, single); break;
+    case kCoeffSub: k_coeff<kCoeffSub><<<grid, T, 0, s>>>(a, n, consts, single); break;
+    case kCoeffMul: k_coeff<kCoeffMul><<<grid, T, 0, s>>>(a, n, consts, single); break;
+    default: return fail(BC_ERR_INTERNAL, "unknown coefficient op");
+    }
+    return check_launch("k_coeff");
 }
 
 int launch_digest(const uint64_t *in, size_t count, uint64_t first, uint64_t *out, cudaStream_t s) {

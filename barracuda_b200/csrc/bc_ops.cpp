@@ -62,6 +62,47 @@ int check_pair(size_t a_len, size_t b_len, uint32_t degree) {
     return BC_OK;
 }
 
+// FhePolyAdd::new (ops/fhe_poly_add.rs:64-101), FhePolySub::new and
+// FhePolyMul::new (fhe_poly_sub.rs, fhe_poly_mul.rs:34-66): both lengths,
+// then the modulus.  (Their same-device check has no counterpart for raw
+// device pointers of one context.)
+int check_coeff_lengths(size_t a_len, size_t b_len, uint32_t degree) {
+    const size_t expected = static_cast<size_t>(degree) * 2;
+    if (a_len != expected)
+        return fail(BC_ERR_DEVICE, format("poly_a length %zu doesn't match expected %zu (degree %u * 2)",
+                                          a_len, expected, degree));
+    if (b_len != expected)
+        return fail(BC_ERR_DEVICE, format("poly_b length %zu doesn't match expected %zu (degree %u * 2)",
+                                          b_len, expected, degree));
+    return BC_OK;
+}
+
+int check_coeff(size_t a_len, size_t b_len, uint32_t degree, uint64_t modulus) {
+    const int st = check_coeff_lengths(a_len, b_len, degree);
+    if (st) return st;
+    if (modulus == 0) return fail(BC_ERR_DEVICE, "Modulus must be non-zero");
+    return BC_OK;
+}
+
+int run_coeff(bc_ctx *ctx, int op, const uint64_t *a, const uint64_t *b, uint32_t degree,
+              uint64_t modulus, uint64_t *out) {
+    if (degree == 0) return BC_OK;
+    if (!a || !b || !out) return fail(BC_ERR_INVALID_INPUT, "device pointers must not be NULL");
+    int st = bc::use_device(ctx);
+    if (st) return st;
+    bc::KArgs k = {};
+    k.in = a;
+    k.in2 = b;
+    k.out = out;
+    k.poly_stride = degree;
+    k.limb_stride = degree;
+    k.batch = 1;
+    k.n_limbs = 1;
+    k.status = ctx->d_status;
+    if ((st = bc::launch_coeff_op(op, k, degree, nullptr, bc::coeff_const(modulus), ctx->stream))) return st;
+    return bc::ctx_sync(ctx);
+}
+
 // Moduli the CUDA path cannot represent (>= 2^62): the reference accepts
 // them but computes truncated products there.
 int check_width(uint64_t modulus) {
@@ -278,6 +319,35 @@ Result<Tensor> FhePointwiseMul::execute() const {
     return out;
 }
 
+template <CoeffKind K>
+Result<FheCoeffOp<K>> FheCoeffOp<K>::create(Tensor a, Tensor b, uint32_t degree, uint64_t modulus) {
+    int st = check_coeff_lengths(a.len(), b.len(), degree);
+    if (!st && a.device() != b.device()) st = fail(BC_ERR_DEVICE, "poly_a and poly_b must be on the same device");
+    if (!st && modulus == 0) st = fail(BC_ERR_DEVICE, "Modulus must be non-zero");
+    if (st) return Result<FheCoeffOp>::err(last(st));
+    FheCoeffOp op;
+    op.a_ = std::move(a);
+    op.b_ = std::move(b);
+    op.degree_ = degree;
+    op.modulus_ = modulus;
+    return Result<FheCoeffOp>::ok(std::move(op));
+}
+
+template <CoeffKind K>
+Result<Tensor> FheCoeffOp<K>::execute() const {
+    auto out = Tensor::empty_u64(degree_, a_.device());
+    if (out.is_err()) return out;
+    const int op = K == CoeffKind::Add ? bc::kCoeffAdd : K == CoeffKind::Sub ? bc::kCoeffSub : bc::kCoeffMul;
+    const int st = run_coeff(a_.device()->ctx(), op, a_.data(), b_.data(), degree_, modulus_,
+                             out.value().mutable_data());
+    if (st) return Result<Tensor>::err(last(st));
+    return out;
+}
+
+template class FheCoeffOp<CoeffKind::Add>;
+template class FheCoeffOp<CoeffKind::Sub>;
+template class FheCoeffOp<CoeffKind::Mul>;
+
 Result<FheFastPolyMul> FheFastPolyMul::create(Tensor a, Tensor b, uint32_t degree, uint64_t modulus,
                                               uint64_t root) {
     const int st = check_pair(a.len(), b.len(), degree);
@@ -371,6 +441,36 @@ int bc_fhe_fast_poly_mul(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, con
     if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
     const int st = check_pair(a_len_u32, b_len_u32, degree);
     return st ? st : run_fast_poly_mul(ctx, d_a, d_b, degree, modulus, root, d_out);
+}
+
+int bc_fhe_poly_add_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree, uint64_t modulus) {
+    return check_coeff(a_len_u32, b_len_u32, degree, modulus);
+}
+int bc_fhe_poly_sub_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree, uint64_t modulus) {
+    return check_coeff(a_len_u32, b_len_u32, degree, modulus);
+}
+int bc_fhe_poly_mul_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree, uint64_t modulus) {
+    return check_coeff(a_len_u32, b_len_u32, degree, modulus);
+}
+
+static int coeff_entry(int op, bc_ctx *ctx, const uint64_t *d_a, size_t a_len, const uint64_t *d_b,
+                       size_t b_len, uint32_t degree, uint64_t modulus, uint64_t *d_out) {
+    if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
+    const int st = check_coeff(a_len, b_len, degree, modulus);
+    return st ? st : run_coeff(ctx, op, d_a, d_b, degree, modulus, d_out);
+}
+
+int bc_fhe_poly_add(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const uint64_t *d_b,
+                    size_t b_len_u32, uint32_t degree, uint64_t modulus, uint64_t *d_out) {
+    return coeff_entry(bc::kCoeffAdd, ctx, d_a, a_len_u32, d_b, b_len_u32, degree, modulus, d_out);
+}
+int bc_fhe_poly_sub(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const uint64_t *d_b,
+                    size_t b_len_u32, uint32_t degree, uint64_t modulus, uint64_t *d_out) {
+    return coeff_entry(bc::kCoeffSub, ctx, d_a, a_len_u32, d_b, b_len_u32, degree, modulus, d_out);
+}
+int bc_fhe_poly_mul(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const uint64_t *d_b,
+                    size_t b_len_u32, uint32_t degree, uint64_t modulus, uint64_t *d_out) {
+    return coeff_entry(bc::kCoeffMul, ctx, d_a, a_len_u32, d_b, b_len_u32, degree, modulus, d_out);
 }
 
 }  // extern "C"

@@ -117,6 +117,24 @@ private:
     uint64_t modulus_ = 0;
 };
 
+// ops/fhe_poly_add.rs:47-175, fhe_poly_sub.rs, fhe_poly_mul.rs: coefficient-
+// wise add / sub / mul.  execute() consumes nothing (the Rust ops take self).
+enum class CoeffKind { Add, Sub, Mul };
+template <CoeffKind K>
+class FheCoeffOp {
+public:
+    static Result<FheCoeffOp> create(Tensor a, Tensor b, uint32_t degree, uint64_t modulus);
+    Result<Tensor> execute() const;
+
+private:
+    Tensor a_, b_;
+    uint32_t degree_ = 0;
+    uint64_t modulus_ = 0;
+};
+using FhePolyAdd = FheCoeffOp<CoeffKind::Add>;
+using FhePolySub = FheCoeffOp<CoeffKind::Sub>;
+using FhePolyMul = FheCoeffOp<CoeffKind::Mul>;
+
 // ops/fhe_fast_poly_mul.rs:39-171.
 class FheFastPolyMul {
 public:

@@ -638,7 +638,13 @@ int bc_plan_create(bc_ctx *ctx, uint32_t degree, uint32_t n_limbs, const uint64_
             }
         }
     }
+    std::vector<CoeffConst> coeff(n_limbs);
+    for (uint32_t l = 0; l < n_limbs; ++l) coeff[l] = coeff_const(p->moduli[l]);
     cudaError_t e = cudaMalloc(&p->d_limbs, sizeof(LimbConst) * n_limbs);
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_coeff, sizeof(CoeffConst) * n_limbs);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(p->d_coeff, coeff.data(), sizeof(CoeffConst) * n_limbs, cudaMemcpyHostToDevice,
+                            ctx->stream);
     if (e == cudaSuccess) e = cudaMalloc(&p->d_tw_fwd, fwd.size());
     if (e == cudaSuccess) e = cudaMalloc(&p->d_tw_inv, inv.size());
     if (e == cudaSuccess && !fwd_fast.empty()) e = cudaMalloc(&p->d_tw_fwd_fast, fwd_fast.size());
@@ -669,6 +675,7 @@ int bc_plan_destroy(bc_plan *p) {
     use_device(p->ctx);
     cudaStreamSynchronize(p->ctx->stream);
     cudaFree(p->d_limbs);
+    cudaFree(p->d_coeff);
     cudaFree(p->d_tw_fwd);
     cudaFree(p->d_tw_inv);
     cudaFree(p->d_tw_fwd_fast);
@@ -710,6 +717,32 @@ int bc_pointwise_mul(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t 
                      const bc_layout *layout, void *stream) {
     if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");
     return run_pointwise(p, a, b, c, batch, layout, pick_stream(p, stream));
+}
+
+static int run_coeff(bc_plan *p, int op, const uint64_t *a_, const uint64_t *b, uint64_t *c,
+                     uint32_t batch, const bc_layout *layout, void *stream) {
+    if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");
+    KArgs a;
+    int st = make_args(p, a_, b, c, batch, layout, &a);
+    if (st) return st;
+    if (!b) return fail(BC_ERR_INVALID_INPUT, "device pointers must not be NULL");
+    if ((st = use_device(p->ctx))) return st;
+    return launch_coeff_op(op, a, p->degree, p->d_coeff, CoeffConst{}, pick_stream(p, stream));
+}
+
+int bc_poly_add(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t batch,
+                const bc_layout *layout, void *stream) {
+    return run_coeff(p, kCoeffAdd, a, b, c, batch, layout, stream);
+}
+
+int bc_poly_sub(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t batch,
+                const bc_layout *layout, void *stream) {
+    return run_coeff(p, kCoeffSub, a, b, c, batch, layout, stream);
+}
+
+int bc_poly_mul(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t batch,
+                const bc_layout *layout, void *stream) {
+    return run_coeff(p, kCoeffMul, a, b, c, batch, layout, stream);
 }
 
 int bc_polymul(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t batch,

@@ -42,6 +42,7 @@ struct bc_plan {
     std::vector<uint64_t> moduli, roots, inv_roots;
     std::vector<bc::LimbConst> limbs;
     bc::LimbConst *d_limbs = nullptr;
+    bc::CoeffConst *d_coeff = nullptr;  // per-limb constants of the coefficient-wise ops
     void *d_tw_fwd = nullptr;  // forward CT table
     void *d_tw_inv = nullptr;  // inverse table (CT for cyclic, GS for negacyclic), N^-1 folded
     void *d_tw_fwd_fast = nullptr;  // the same tables in the fast kernels' layout

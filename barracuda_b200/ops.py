@@ -186,6 +186,47 @@ class FhePointwiseMul:
         return out
 
 
+class _FheCoeffOp:
+    """Coefficient-wise op of the reference's FHE API; subclasses name the C entry point."""
+    _name = ""
+
+    def __init__(self, poly_a: FheTensor, poly_b: FheTensor, degree: int, modulus: int):
+        L = lib()
+        # same order as the Rust constructors: lengths, same device, modulus
+        st = getattr(L, f"bc_fhe_poly_{self._name}_check")(poly_a.len(), poly_b.len(), degree, 1)
+        check(st)
+        if poly_a.device is not poly_b.device:
+            raise BarracudaError(N.BC_ERR_DEVICE, "poly_a and poly_b must be on the same device")
+        check(getattr(L, f"bc_fhe_poly_{self._name}_check")(poly_a.len(), poly_b.len(), degree, modulus))
+        self.poly_a, self.poly_b, self.degree, self.modulus = poly_a, poly_b, degree, modulus
+
+    @classmethod
+    def new(cls, poly_a, poly_b, degree, modulus):
+        return cls(poly_a, poly_b, degree, modulus)
+
+    def execute(self) -> FheTensor:
+        out = FheTensor(self.poly_a.device, 2 * self.degree)
+        check(getattr(lib(), f"bc_fhe_poly_{self._name}")(
+            self.poly_a.device.handle, self.poly_a.ptr, self.poly_a.len(), self.poly_b.ptr,
+            self.poly_b.len(), self.degree, self.modulus, out.ptr))
+        return out
+
+
+class FhePolyAdd(_FheCoeffOp):
+    """ops/fhe_poly_add.rs:47-175: (a + b) mod q per coefficient."""
+    _name = "add"
+
+
+class FhePolySub(_FheCoeffOp):
+    """ops/fhe_poly_sub.rs: (a - b) mod q per coefficient."""
+    _name = "sub"
+
+
+class FhePolyMul(_FheCoeffOp):
+    """ops/fhe_poly_mul.rs:34-133: (a * b) mod q per coefficient, exact."""
+    _name = "mul"
+
+
 class FheFastPolyMul:
     """ops/fhe_fast_poly_mul.rs:39-171; execute() runs one fused kernel."""
 

@@ -105,6 +105,18 @@ class NttPlan:
         check(lib().bc_pointwise_mul(self.handle, _ptr(a), _ptr(b), _ptr(c), batch,
                                      self._layout(layout), stream or None))
 
+    def poly_add(self, a, b, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
+        check(lib().bc_poly_add(self.handle, _ptr(a), _ptr(b), _ptr(c), batch, self._layout(layout),
+                                stream or None))
+
+    def poly_sub(self, a, b, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
+        check(lib().bc_poly_sub(self.handle, _ptr(a), _ptr(b), _ptr(c), batch, self._layout(layout),
+                                stream or None))
+
+    def poly_mul(self, a, b, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
+        check(lib().bc_poly_mul(self.handle, _ptr(a), _ptr(b), _ptr(c), batch, self._layout(layout),
+                                stream or None))
+
     def polymul(self, a, b, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
         check(lib().bc_polymul(self.handle, _ptr(a), _ptr(b), _ptr(c), batch, self._layout(layout),
                                stream or None))

@@ -454,6 +454,36 @@ def run_sweep(args):
         print(json.dumps(line), flush=True)
         del x, y
         plan.close()
+    # coefficient-wise ops (FhePolyAdd / FhePolySub / FhePolyMul semantics), 24 bytes
+    # per coefficient (read a, b; write c), both prime families
+    for bits in (31, 60):
+        n, limbs = 1 << 16, 16
+        batch = (1 << 28) // (n * limbs)
+        qs = bc.ntt_primes(bits, n, limbs)
+        plan = bc.NttPlan(dev, n, qs, [bc.negacyclic_root(q, n) for q in qs], mode=bc.NEGACYCLIC)
+        a = torch.empty(limbs * batch * n, dtype=torch.int64, device="cuda")
+        b, c = torch.empty_like(a), torch.empty_like(a)
+        plan.fill_uniform(a, batch, seed=1, stream=sh)
+        plan.fill_uniform(b, batch, seed=2, stream=sh)
+        line = {"sweep": "coefficient ops, 1 GPU", "N": n, "limbs": limbs, "batch": batch, "bits": bits,
+                "peak_gbs": hbm, "peak_kind": peak_kind}
+        for name in ("poly_add", "poly_sub", "poly_mul"):
+            fn = getattr(plan, name)
+            for _ in range(args.warmup):
+                fn(a, b, c, batch, stream=sh)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn(a, b, c, batch, stream=sh)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            gbs = limbs * batch * 24 * n / (ms / 1000.0) / 1e9
+            line[name] = {"ms": ms, "gb_per_s": gbs, "frac": gbs / hbm}
+        print(json.dumps(line), flush=True)
+        del a, b, c
+        plan.close()
     dev.close()
 
 

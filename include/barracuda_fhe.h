@@ -14,6 +14,8 @@
  *   - ops/fhe_intt/mod.rs:82 FheIntt::new, compute.rs:27     -> bc_fhe_intt*
  *   - ops/fhe_pointwise_mul.rs:64,119 FhePointwiseMul        -> bc_fhe_pointwise_mul*
  *   - ops/fhe_fast_poly_mul.rs:61,122 FheFastPolyMul         -> bc_fhe_fast_poly_mul*
+ *   - ops/fhe_poly_add.rs:64,128 FhePolyAdd, fhe_poly_sub.rs FhePolySub,
+ *     fhe_poly_mul.rs:34,82 FhePolyMul                       -> bc_fhe_poly_{add,sub,mul}*
  *   - ops/fhe_ntt/mod.rs:210 compute_primitive_root          -> bc_compute_primitive_root
  *   - ops/fhe_intt/mod.rs:202 compute_inverse_root           -> bc_compute_inverse_root
  *   - ops/fhe_poly_add.rs:185 create_fhe_poly_tensor,
@@ -135,6 +137,23 @@ int bc_fhe_fast_poly_mul(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32,
                          const uint64_t *d_b, size_t b_len_u32, uint32_t degree,
                          uint64_t modulus, uint64_t root_of_unity, uint64_t *d_out);
 
+/* ops/fhe_poly_add.rs:64-175, fhe_poly_sub.rs, fhe_poly_mul.rs:34-133:
+ * coefficient-wise C = A + B, A - B, A * B modulo q (any degree; same checks
+ * and message text as the Rust constructors).  Add and sub reproduce the
+ * reference bit for bit for any u64 inputs (a wrapping sum minus q at most
+ * twice; a - b, or (q - b) + a when a < b).  Mul returns the exact residue
+ * (a * b) mod q; the reference's shader matches it only while its product
+ * stays below 1001 q and its 32x32 partial products do not overflow. */
+int bc_fhe_poly_add_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree, uint64_t modulus);
+int bc_fhe_poly_add(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const uint64_t *d_b,
+                    size_t b_len_u32, uint32_t degree, uint64_t modulus, uint64_t *d_out);
+int bc_fhe_poly_sub_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree, uint64_t modulus);
+int bc_fhe_poly_sub(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const uint64_t *d_b,
+                    size_t b_len_u32, uint32_t degree, uint64_t modulus, uint64_t *d_out);
+int bc_fhe_poly_mul_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree, uint64_t modulus);
+int bc_fhe_poly_mul(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const uint64_t *d_b,
+                    size_t b_len_u32, uint32_t degree, uint64_t modulus, uint64_t *d_out);
+
 /* ------------------------------------------------ batched plans (new path)
  * A plan holds, for n_limbs RNS limbs of one degree N, the device twiddle
  * tables (with Shoup companions), N^-1 and the kernel choice.
@@ -182,6 +201,14 @@ int bc_ntt_forward(bc_plan *plan, const uint64_t *d_in, uint64_t *d_out, uint32_
                    const bc_layout *layout, void *stream);
 int bc_ntt_inverse(bc_plan *plan, const uint64_t *d_in, uint64_t *d_out, uint32_t batch,
                    const bc_layout *layout, void *stream);
+/* Coefficient-wise C = A + B, A - B, A * B mod q_l over the whole batch,
+ * with the semantics of bc_fhe_poly_add / _sub / _mul (inputs any u64). */
+int bc_poly_add(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
+                uint32_t batch, const bc_layout *layout, void *stream);
+int bc_poly_sub(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
+                uint32_t batch, const bc_layout *layout, void *stream);
+int bc_poly_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
+                uint32_t batch, const bc_layout *layout, void *stream);
 /* C = A * B mod q_l, coefficient-wise. */
 int bc_pointwise_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                      uint32_t batch, const bc_layout *layout, void *stream);

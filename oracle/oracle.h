@@ -77,6 +77,20 @@ void orc_ref_negacyclic_ntt(const uint64_t *in, uint64_t *out, uint32_t degree,
 void orc_ref_negacyclic_intt(const uint64_t *in, uint64_t *out, uint32_t degree,
                              uint64_t modulus, uint64_t psi);
 
+/* Coefficient-wise ops (ref_poly.c), reference behaviour for any u64 input:
+ * fhe_poly_add.wgsl (wrapping sum, two conditional subtractions of q),
+ * fhe_poly_sub.wgsl (a - b, or (q - b) + a when a < b), fhe_poly_mul.wgsl
+ * (128-bit product through a 32x32 helper that can lose 2^32 in its middle
+ * sum, then at most 1000 subtractions of q, or an approximate Barrett step
+ * above 2^64).  orc_exact_poly_mul is the exact (a * b) mod q. */
+uint64_t orc_ref_poly_add1(uint64_t a, uint64_t b, uint64_t q);
+uint64_t orc_ref_poly_sub1(uint64_t a, uint64_t b, uint64_t q);
+uint64_t orc_ref_poly_mul1(uint64_t a, uint64_t b, uint64_t q);
+void orc_ref_poly_add(const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t degree, uint64_t q);
+void orc_ref_poly_sub(const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t degree, uint64_t q);
+void orc_ref_poly_mul(const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t degree, uint64_t q);
+void orc_exact_poly_mul(const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t degree, uint64_t q);
+
 /* ---------------- part 2: exact arithmetic ---------------- */
 
 uint64_t orc_mulmod(uint64_t a, uint64_t b, uint64_t q);

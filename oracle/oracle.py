@@ -35,7 +35,7 @@ def _stale() -> bool:
     if not os.path.exists(_SO):
         return True
     t = os.path.getmtime(_SO)
-    srcs = [os.path.join(_HERE, f) for f in ("ref_wgsl.c", "exact.c", "baseline.c", "oracle.h")]
+    srcs = [os.path.join(_HERE, f) for f in ("ref_wgsl.c", "ref_poly.c", "exact.c", "baseline.c", "oracle.h")]
     return any(os.path.exists(f) and os.path.getmtime(f) > t for f in srcs)
 
 
@@ -78,6 +78,13 @@ def lib():
             "orc_seeded_value": (u64, [u64, u64, u64]),
             "orc_seeded_fill": (None, [_u64p, ctypes.c_size_t, u64, u64, u64]),
             "orc_digest": (u64, [_u64p, ctypes.c_size_t, u64]),
+            "orc_ref_poly_add1": (u64, [u64, u64, u64]),
+            "orc_ref_poly_sub1": (u64, [u64, u64, u64]),
+            "orc_ref_poly_mul1": (u64, [u64, u64, u64]),
+            "orc_ref_poly_add": (None, [_u64p, _u64p, _u64p, u32, u64]),
+            "orc_ref_poly_sub": (None, [_u64p, _u64p, _u64p, u32, u64]),
+            "orc_ref_poly_mul": (None, [_u64p, _u64p, _u64p, u32, u64]),
+            "orc_exact_poly_mul": (None, [_u64p, _u64p, _u64p, u32, u64]),
             "orc_baseline_run": (ctypes.c_double,
                                  [i32, _u64p, _u64p, u32, u32, _u64p, _u64p, u32, i32]),
         }
@@ -175,6 +182,33 @@ def seeded_fill(count, seed, g0, q):
     out = np.zeros(count, dtype=np.uint64)
     lib().orc_seeded_fill(_p(out), count, seed, g0, q)
     return out
+
+
+def _binary(fname, a, b, q):
+    a, b = _arr(a), _arr(b)
+    assert a.size == b.size
+    out = np.zeros(a.size, dtype=np.uint64)
+    getattr(lib(), fname)(_p(a), _p(b), _p(out), a.size, q)
+    return out
+
+
+def ref_poly_add(a, b, q):
+    """FhePolyAdd::execute (ops/fhe_poly_add.rs:128-175, fhe_poly_add.wgsl)."""
+    return _binary("orc_ref_poly_add", a, b, q)
+
+
+def ref_poly_sub(a, b, q):
+    """FhePolySub::execute (ops/fhe_poly_sub.rs, fhe_poly_sub.wgsl)."""
+    return _binary("orc_ref_poly_sub", a, b, q)
+
+
+def ref_poly_mul(a, b, q):
+    """FhePolyMul::execute (ops/fhe_poly_mul.rs:82-133, fhe_poly_mul.wgsl)."""
+    return _binary("orc_ref_poly_mul", a, b, q)
+
+
+def exact_poly_mul(a, b, q):
+    return _binary("orc_exact_poly_mul", a, b, q)
 
 
 def digest(x, first_index=0):

@@ -69,6 +69,30 @@ CASES = [
     {"name": "fast_mul_distributive_4_12289", "kind": "fast_mul_distributive", "degree": 4,
      "modulus": 12289, "root": "find_root_of_unity",
      "source": "crates/barracuda/tests/fhe/fast_poly_mul.rs:112-170"},
+    {"name": "poly_add_8_97", "kind": "poly_add", "degree": 8, "modulus": 97,
+     "a": [1, 2, 3, 4, 5, 6, 7, 8], "b": [10, 20, 30, 40, 50, 60, 70, 80],
+     "expect": [11, 22, 33, 44, 55, 66, 77, 88],
+     "source": "crates/barracuda/src/ops/fhe_poly_add.rs:203-251"},
+    {"name": "poly_add_reduce_4_100", "kind": "poly_add", "degree": 4, "modulus": 100,
+     "a": [50, 60, 70, 80], "b": [60, 50, 40, 30], "expect": [10, 10, 10, 10],
+     "source": "crates/barracuda/src/ops/fhe_poly_add.rs:254-302"},
+    {"name": "poly_sub_8_97", "kind": "poly_sub", "degree": 8, "modulus": 97,
+     "a": [50, 60, 70, 80, 90, 85, 75, 65], "b": [10, 20, 30, 40, 50, 60, 70, 80],
+     "expect": [40, 40, 40, 40, 40, 25, 5, 82],
+     "source": "crates/barracuda/src/ops/fhe_poly_sub.rs:171-217"},
+    {"name": "poly_mul_8_97", "kind": "poly_mul", "degree": 8, "modulus": 97,
+     "a": [2, 3, 4, 5, 6, 7, 8, 9], "b": [5, 4, 3, 2, 10, 10, 10, 10],
+     "expect": [10, 12, 12, 10, 60, 70, 80, 90],
+     "source": "crates/barracuda/src/ops/fhe_poly_mul.rs:160-205"},
+    {"name": "poly_add_prop_4_257", "kind": "poly_add", "degree": 4, "modulus": 257,
+     "a": [10, 20, 30, 40], "b": [5, 15, 25, 35], "expect": [15, 35, 55, 75],
+     "source": "crates/barracuda/tests/property/fhe_properties.rs:266-291 (expected from the test's mod_add)"},
+    {"name": "poly_sub_prop_4_257", "kind": "poly_sub", "degree": 4, "modulus": 257,
+     "a": [40, 30, 20, 10], "b": [5, 15, 25, 35], "expect": [35, 15, 252, 232],
+     "source": "crates/barracuda/tests/property/fhe_properties.rs:293-318 (expected from the test's mod_sub)"},
+    {"name": "poly_add_assoc_4_257", "kind": "poly_add_assoc", "degree": 4, "modulus": 257,
+     "a": [10, 20, 30, 40], "b": [5, 15, 25, 35], "c": [3, 7, 11, 13],
+     "source": "crates/barracuda/tests/property/fhe_properties.rs:320-365"},
 ]
 
 # tests/fhe/helpers.rs:21-28 -- (degree, modulus, root), all primitive roots

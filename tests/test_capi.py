@@ -58,6 +58,21 @@ def test_fhe_ntt_validation_messages():
     assert L.bc_fhe_ntt_check(8, 4, 1, 0) == 0
 
 
+@pytest.mark.parametrize("op", ["add", "sub", "mul"])
+def test_fhe_poly_coeff_validation_messages(op):
+    """FhePolyAdd/Sub/Mul::new (ops/fhe_poly_{add,sub,mul}.rs): lengths, then modulus."""
+    L = N.lib()
+    f = getattr(L, f"bc_fhe_poly_{op}_check")
+    assert _check_msg(f, 14, 16, 8, 97) == (
+        N.BC_ERR_DEVICE, "poly_a length 14 doesn't match expected 16 (degree 8 * 2)")
+    assert _check_msg(f, 16, 10, 8, 97) == (
+        N.BC_ERR_DEVICE, "poly_b length 10 doesn't match expected 16 (degree 8 * 2)")
+    assert _check_msg(f, 16, 16, 8, 0) == (N.BC_ERR_DEVICE, "Modulus must be non-zero")
+    assert f(16, 16, 8, 97) == 0
+    assert f(6, 6, 3, 100) == 0  # no power-of-two or prime requirement
+    assert f(0, 0, 0, 5) == 0
+
+
 def test_fhe_intt_validation_messages():
     L = N.lib()
     assert _check_msg(L.bc_fhe_intt_check, 6, 4, 17, 13) == (

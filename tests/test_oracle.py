@@ -30,8 +30,9 @@ def test_golden_cases(kats):
             n, q = c["degree"], c["modulus"]
             r = resolve_root(c["root"], n, q)
             a, b = np.array(c["a"], np.uint64), np.array(c["b"], np.uint64)
-            lhs = O.ref_ntt((a + b) % np.uint64(q), n, q, r)
-            rhs = (O.ref_ntt(a, n, q, r) + O.ref_ntt(b, n, q, r)) % np.uint64(q)
+            # NTT(FhePolyAdd(a, b)) == FhePolyAdd(NTT(a), NTT(b))
+            lhs = O.ref_ntt(O.ref_poly_add(a, b, q), n, q, r)
+            rhs = O.ref_poly_add(O.ref_ntt(a, n, q, r), O.ref_ntt(b, n, q, r), q)
             assert (lhs == rhs).all()
         elif k == "ntt_zero":
             n, q = c["degree"], c["modulus"]
@@ -72,6 +73,16 @@ def test_golden_cases(kats):
             lhs = O.ref_fast_poly_mul(a, (b + cc) % np.uint64(q), n, q, r)
             rhs = (O.ref_fast_poly_mul(a, b, n, q, r) + O.ref_fast_poly_mul(a, cc, n, q, r)) % np.uint64(q)
             assert (lhs == rhs).all()
+        elif k in ("poly_add", "poly_sub", "poly_mul"):
+            f = {"poly_add": O.ref_poly_add, "poly_sub": O.ref_poly_sub, "poly_mul": O.ref_poly_mul}[k]
+            assert list(f(c["a"], c["b"], c["modulus"])) == c["expect"], c["name"]
+            if k == "poly_mul":
+                assert list(O.exact_poly_mul(c["a"], c["b"], c["modulus"])) == c["expect"], c["name"]
+        elif k == "poly_add_assoc":
+            q = c["modulus"]
+            a, b, cc = c["a"], c["b"], c["c"]
+            lhs = O.ref_poly_add(O.ref_poly_add(a, b, q), cc, q)
+            assert (lhs == O.ref_poly_add(a, O.ref_poly_add(b, cc, q), q)).all()
         else:
             raise AssertionError(f"unknown kind {k}")
 
@@ -188,3 +199,26 @@ def test_seeded_generator_uniform_range():
     assert (v < q).all()
     assert abs(float(v.mean()) / q - 0.5) < 0.01
     assert O.seeded_fill(8, 5, 100, q).tolist() == [L.orc_seeded_value(5, 100 + i, q) for i in range(8)]
+
+
+def test_poly_ops_restatement_vs_exact():
+    """FhePolyAdd/Sub match (a +- b) mod q for reduced inputs; FhePolyMul's
+    shader matches the exact product only while a * b < 1001 q and its 32x32
+    partial products do not overflow, which the reference's own tests stay
+    within.  The CUDA path computes the exact residue everywhere."""
+    rng = np.random.default_rng(3)
+    for q in (97, 100, 12289, 2147352577, 1152921504606584833):
+        a = rng.integers(0, q, 2000, dtype=np.uint64)
+        b = rng.integers(0, q, 2000, dtype=np.uint64)
+        add = np.array([(int(x) + int(y)) % q for x, y in zip(a, b)], np.uint64)
+        sub = np.array([(int(x) - int(y)) % q for x, y in zip(a, b)], np.uint64)
+        assert (O.ref_poly_add(a, b, q) == add).all()
+        assert (O.ref_poly_sub(a, b, q) == sub).all()
+        exact = np.array([int(x) * int(y) % q for x, y in zip(a, b)], np.uint64)
+        assert (O.exact_poly_mul(a, b, q) == exact).all()
+        small = rng.integers(0, 31, 2000, dtype=np.uint64) % np.uint64(q)  # a * b < 1001 q
+        assert (O.ref_poly_mul(small, small, q) == O.exact_poly_mul(small, small, q)).all()
+    # divergence pinned: operands near a 31-bit modulus leave the shader's range
+    q = 2147352577
+    a = np.array([q - 1, q - 2, 123456789], np.uint64)
+    assert (O.ref_poly_mul(a, a, q) != O.exact_poly_mul(a, a, q)).all()

@@ -30,6 +30,11 @@ def intt(dev, x, n, q, r):
     return np.array(bc.FheIntt.new(upload(dev, x), n, q, r).execute().to_u64())
 
 
+def coeff_op(dev, op, a, b, n, q):
+    cls = {"add": bc.FhePolyAdd, "sub": bc.FhePolySub, "mul": bc.FhePolyMul}[op]
+    return np.array(cls.new(upload(dev, a), upload(dev, b), n, q).execute().to_u64())
+
+
 # ------------------------------------------------------------ reference ops
 
 def test_golden_cases_on_gpu(device, kats):
@@ -47,8 +52,17 @@ def test_golden_cases_on_gpu(device, kats):
             n, q = c["degree"], c["modulus"]
             r = resolve_root(c["root"], n, q)
             a, b = np.array(c["a"], np.uint64), np.array(c["b"], np.uint64)
-            lhs = ntt(device, (a + b) % np.uint64(q), n, q, r)
-            assert (lhs == (ntt(device, a, n, q, r) + ntt(device, b, n, q, r)) % np.uint64(q)).all()
+            lhs = ntt(device, coeff_op(device, "add", a, b, n, q), n, q, r)
+            rhs = coeff_op(device, "add", ntt(device, a, n, q, r), ntt(device, b, n, q, r), n, q)
+            assert (lhs == rhs).all()
+        elif k in ("poly_add", "poly_sub", "poly_mul"):
+            got = coeff_op(device, k[5:], c["a"], c["b"], c["degree"], c["modulus"])
+            assert list(got) == c["expect"], name
+        elif k == "poly_add_assoc":
+            n, q = c["degree"], c["modulus"]
+            a, b, cc = c["a"], c["b"], c["c"]
+            lhs = coeff_op(device, "add", coeff_op(device, "add", a, b, n, q), cc, n, q)
+            assert (lhs == coeff_op(device, "add", a, coeff_op(device, "add", b, cc, n, q), n, q)).all()
         elif k == "ntt_zero":
             n, q = c["degree"], c["modulus"]
             assert (ntt(device, c["input"], n, q, resolve_root(c["root"], n, q)) == 0).all()
@@ -383,3 +397,56 @@ def test_digest_matches_oracle_and_adds_over_shards(device):
         got.append(int(out.to_u64()[0]))
         assert got[-1] == O.digest(x[lo:hi], first)
     assert got[0] == (got[1] + got[2]) % 2**64
+
+
+# ------------------------------------------------------- coefficient-wise ops
+
+COEFF_MODULI = [1, 97, 100, 12289, 2147352577, 4294967291, 1152921504606584833,
+                (1 << 63) + 29, (1 << 64) - 59]
+
+
+def _coeff_inputs(rng, n, q):
+    """Reduced values, arbitrary u64 words, and values next to 2^64 (wrap-around)."""
+    top = np.uint64(2**64 - 1)
+    parts = [rng.integers(0, q, n // 2, dtype=np.uint64, endpoint=False) if q > 1 else np.zeros(n // 2, np.uint64),
+             rng.integers(0, 2**64 - 1, n // 4, dtype=np.uint64, endpoint=True),
+             top - rng.integers(0, 1000, n - n // 2 - n // 4, dtype=np.uint64)]
+    x = np.concatenate(parts)
+    rng.shuffle(x)
+    return x
+
+
+@pytest.mark.parametrize("q", COEFF_MODULI)
+def test_coeff_ops_match_reference_and_exact(device, q):
+    """FhePolyAdd / FhePolySub: bit-exact with the reference's shaders for any
+    u64 inputs; FhePolyMul: the exact residue (a * b) mod q.  Degree 1000
+    (the ops take any degree)."""
+    n = 1000
+    rng = np.random.default_rng(q % 1000003)
+    a, b = _coeff_inputs(rng, n, q), _coeff_inputs(rng, n, q)
+    assert (coeff_op(device, "add", a, b, n, q) == O.ref_poly_add(a, b, q)).all()
+    assert (coeff_op(device, "sub", a, b, n, q) == O.ref_poly_sub(a, b, q)).all()
+    assert (coeff_op(device, "mul", a, b, n, q) == O.exact_poly_mul(a, b, q)).all()
+
+
+@pytest.mark.parametrize("bits", [31, 60])
+def test_plan_coeff_ops(device, bits):
+    """Batched bc_poly_add / _sub / _mul over limbs x polynomials, strided layout."""
+    n, limbs, batch = 1 << 12, 3, 5
+    plan, qs, _ = _plan(device, n, limbs, bits, bc.NEGACYCLIC)
+    lay = bc.Layout(limb_stride=n, poly_stride=limbs * n)  # [poly][limb][N]
+    total = limbs * batch * n
+    rng = np.random.default_rng(bits)
+    A = rng.integers(0, 2**64 - 1, total, dtype=np.uint64, endpoint=True)
+    B = rng.integers(0, 2**64 - 1, total, dtype=np.uint64, endpoint=True)
+    A[: total // 2] %= np.uint64(qs[0])
+    a, b, c = upload(device, A), upload(device, B), _alloc(device, total)
+    for op, ref in (("add", O.ref_poly_add), ("sub", O.ref_poly_sub), ("mul", O.exact_poly_mul)):
+        getattr(plan, f"poly_{op}")(a, b, c, batch, layout=lay)
+        device.synchronize()
+        C = c.to_u64()
+        for p in range(batch):
+            for l in range(limbs):
+                o = (p * limbs + l) * n
+                assert (C[o:o + n] == ref(A[o:o + n], B[o:o + n], qs[l])).all(), (op, p, l)
+    plan.close()
