@@ -450,3 +450,37 @@ def test_plan_coeff_ops(device, bits):
                 o = (p * limbs + l) * n
                 assert (C[o:o + n] == ref(A[o:o + n], B[o:o + n], qs[l])).all(), (op, p, l)
     plan.close()
+
+
+# ------------------------------------------------------------- IPC methods
+
+def test_ipc_fhe_methods_on_gpu(device):
+    """fhe.ntt / fhe.intt / fhe.pointwise_mul over the NDJSON transport, against
+    the reference's known vector and the oracle."""
+    from barracuda_b200 import ipc
+    srv = ipc.FheIpc(device).serve_tcp("127.0.0.1", 0)
+    try:
+        r = ipc.call(srv.server_address, {"jsonrpc": "2.0", "method": "barracuda.fhe.ntt", "id": 1,
+                                          "params": {"modulus": 17, "degree": 4, "root_of_unity": 4,
+                                                     "coefficients": [1, 2, 3, 4]}})
+        assert r == {"jsonrpc": "2.0", "id": 1, "result": {"degree": 4, "modulus": 17, "result": [10, 7, 15, 6],
+                                                            "status": "completed"}}
+        r = ipc.call(srv.server_address, {"jsonrpc": "2.0", "method": "fhe.intt", "id": 2,
+                                          "params": {"modulus": 17, "degree": 4, "inv_root_of_unity": 13,
+                                                     "coefficients": [10, 7, 15, 6]}})
+        assert r["result"]["result"] == [1, 2, 3, 4]
+        n, q = 64, 12289
+        rng = np.random.default_rng(5)
+        a, b = random_poly(rng, n, q), random_poly(rng, n, q)
+        r = ipc.call(srv.server_address, {"jsonrpc": "2.0", "method": "fhe.pointwise_mul", "id": 3,
+                                          "params": {"modulus": q, "degree": n, "a": [int(v) for v in a],
+                                                     "b": [int(v) for v in b]}})
+        assert r["result"]["result"] == [int(v) for v in O.ref_pointwise(a, b, n, q)]
+        r = ipc.call(srv.server_address, {"jsonrpc": "2.0", "method": "fhe.ntt", "id": 4,
+                                          "params": {"modulus": 19, "degree": 8, "root_of_unity": 2,
+                                                     "coefficients": list(range(8))}})
+        assert r["error"] == {"code": ipc.INTERNAL_ERROR, "message":
+                              "NTT setup failed: Device error: Modulus 19 must satisfy q ≡ 1 (mod 2N) where N=8"}
+    finally:
+        srv.shutdown()
+        srv.server_close()
