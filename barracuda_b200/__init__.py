@@ -10,9 +10,10 @@ from ._native import BarracudaError, NativeLibraryMissing, LIB_PATH  # noqa: F40
 from .ops import (  # noqa: F401
     Device, FheTensor, create_fhe_poly_tensor, read_poly_from_tensor, compute_primitive_root,
     compute_inverse_root, FheNtt, FheIntt, FhePointwiseMul, FheFastPolyMul, FhePolyAdd, FhePolySub,
-    FhePolyMul,
+    FhePolyMul, FheRotate, FheModulusSwitch, FheKeySwitch, rotation_galois,
 )
 from .plan import (  # noqa: F401
     NttPlan, Layout, CYCLIC, NEGACYCLIC, ntt_prime, ntt_primes, negacyclic_root, partition, digest,
+    modulus_switch, decompose,
 )
 from .shard import Shard, ShardGroup, ShardFailure, job_digest  # noqa: F401

@@ -109,6 +109,13 @@ SIGNATURES = {
     "bc_fhe_poly_mul_check": (_i32, [_sz, _sz, _u32, _u64]),
     "bc_fhe_poly_mul": (_i32, [_vp, _vp, _sz, _vp, _sz, _u32, _u64, _vp]),
     "bc_fhe_fast_poly_mul": (_i32, [_vp, _vp, _sz, _vp, _sz, _u32, _u64, _u64, _vp]),
+    "bc_fhe_rotate_check": (_i32, [_sz, _u32, _i32, _u64]),
+    "bc_fhe_rotate": (_i32, [_vp, _vp, _sz, _u32, _i32, _u64, _vp]),
+    "bc_rotation_galois": (_u32, [_u32, _i32]),
+    "bc_fhe_modulus_switch_check": (_i32, [_sz, _u32, _u64, _u64]),
+    "bc_fhe_modulus_switch": (_i32, [_vp, _vp, _sz, _u32, _u64, _u64, _vp]),
+    "bc_fhe_key_switch_check": (_i32, [_sz, _u32, _u64, _u32, _u32]),
+    "bc_fhe_key_switch": (_i32, [_vp, _vp, _sz, _u32, _u64, _u32, _u32, _vp]),
     "bc_plan_create": (_i32, [_vp, _u32, _u32, _u64p, _u64p, _u64p, _i32, ctypes.POINTER(_vp)]),
     "bc_plan_destroy": (_i32, [_vp]),
     "bc_plan_info_get": (_i32, [_vp, ctypes.POINTER(bc_plan_info)]),
@@ -120,6 +127,9 @@ SIGNATURES = {
     "bc_pointwise_mul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_polymul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_polymul_static_scratch": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
+    "bc_automorphism": (_i32, [_vp, _vp, _vp, _u32, _lay, _u32, _vp]),
+    "bc_modulus_switch": (_i32, [_vp, _vp, _vp, _sz, _u64, _u64, _vp]),
+    "bc_decompose": (_i32, [_vp, _vp, _vp, _sz, _u32, _u32, _vp]),
     "bc_fill_uniform": (_i32, [_vp, _vp, _u32, _lay, _u64, _u64, _u64, _vp]),
     "bc_digest": (_i32, [_vp, _vp, _sz, _u64, _vp, _vp]),
     "bc_partition": (_i32, [_u64, _u32, _u32, _u64p, _u64p]),

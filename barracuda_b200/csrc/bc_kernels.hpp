@@ -101,4 +101,25 @@ int launch_fill_uniform(const KArgs &a, uint64_t seed, uint64_t first_poly,
                         uint64_t total_polys, cudaStream_t s);
 int launch_digest(const uint64_t *in, size_t count, uint64_t first, uint64_t *out, cudaStream_t s);
 
+// ---- automorphisms, modulus switching, digit decomposition (bc_kernels_rns.cu) ----
+// X -> X^galois (galois odd) on a.batch polynomials of each of a.n_limbs
+// limbs: out[j] = in[t] if t < N, else q - in[t - N] (0 stays 0), where
+// t = j galois^-1 mod 2N; the modulus of limb l is consts[l].q, or single_q
+// when consts is NULL.  a.in and a.out must not overlap.
+int launch_automorphism(const KArgs &a, uint32_t galois, const CoeffConst *consts, uint64_t single_q,
+                        cudaStream_t s);
+// Inverse of an odd g modulo 2^logm (logm <= 32).
+uint32_t odd_inverse_pow2(uint32_t g, uint32_t logm);
+// Constants of round(c q_new / q_old) mod q_new: m_old = floor(2^64 / q_old),
+// p_shoup = floor(q_new 2^64 / q_old); both 0 when q_new == 0.
+struct ModSwitchConst {
+    uint64_t q_old, q_new, m_old, p_shoup;
+};
+ModSwitchConst modswitch_const(uint64_t q_old, uint64_t q_new);  // q_new < q_old
+int launch_modulus_switch(const uint64_t *in, uint64_t *out, size_t count, const ModSwitchConst &c,
+                          cudaStream_t s);
+// out[l * count + i] = digit l (base `base`, 2 <= base <= 2^24) of in[i], l < levels.
+int launch_decompose(const uint64_t *in, uint64_t *out, size_t count, uint32_t base, uint32_t levels,
+                     cudaStream_t s);
+
 }  // namespace bc

@@ -103,6 +103,113 @@ int run_coeff(bc_ctx *ctx, int op, const uint64_t *a, const uint64_t *b, uint32_
     return bc::ctx_sync(ctx);
 }
 
+// FheRotate::new, FheModulusSwitch::new and FheKeySwitch::new share the
+// degree and input-length checks (ops/fhe_rotate.rs:92-113,
+// fhe_modulus_switch.rs:86-107, fhe_key_switch.rs:108-139), all InvalidInput.
+int check_degree4(uint32_t degree) {
+    if (!bc::is_pow2(degree) || degree < 4)
+        return fail(BC_ERR_INVALID_INPUT, format("Degree must be power of 2 >= 4, got %u", degree));
+    return BC_OK;
+}
+
+int check_input_len(size_t len_u32, uint32_t degree) {
+    const size_t expected = static_cast<size_t>(degree) * 2;
+    if (len_u32 != expected)
+        return fail(BC_ERR_INVALID_INPUT,
+                    format("Input must have %zu elements (degree=%u, u64 emulated), got %zu", expected, degree,
+                           len_u32));
+    return BC_OK;
+}
+
+// fhe_rotate.rs:92-113.  |rotation| is taken in 64 bits, so INT32_MIN is
+// out of range (Rust's i32::abs overflows there).
+int check_rotate(size_t len_u32, uint32_t degree, int32_t rotation) {
+    int st = check_degree4(degree);
+    if (st) return st;
+    const int64_t max_rotation = degree / 2;
+    const int64_t mag = rotation < 0 ? -static_cast<int64_t>(rotation) : rotation;
+    if (mag > max_rotation)
+        return fail(BC_ERR_INVALID_INPUT,
+                    format("Rotation %d out of range [-%lld, %lld] for degree %u", rotation,
+                           static_cast<long long>(max_rotation), static_cast<long long>(max_rotation), degree));
+    return check_input_len(len_u32, degree);
+}
+
+// fhe_modulus_switch.rs:86-107.
+int check_modulus_switch(size_t len_u32, uint32_t degree, uint64_t modulus_old, uint64_t modulus_new) {
+    int st = check_degree4(degree);
+    if (st) return st;
+    if (modulus_new >= modulus_old)
+        return fail(BC_ERR_INVALID_INPUT, format("New modulus (%llu) must be < old modulus (%llu)",
+                                                 static_cast<unsigned long long>(modulus_new),
+                                                 static_cast<unsigned long long>(modulus_old)));
+    return check_input_len(len_u32, degree);
+}
+
+// fhe_key_switch.rs:108-139.
+int check_key_switch(size_t len_u32, uint32_t degree, uint32_t decomp_base, uint32_t decomp_levels) {
+    int st = check_degree4(degree);
+    if (st) return st;
+    if (decomp_base < 2 || decomp_base > (1u << 24))
+        return fail(BC_ERR_INVALID_INPUT, format("Decomposition base must be in [2, 2^24], got %u", decomp_base));
+    if (decomp_levels == 0 || decomp_levels > 32)
+        return fail(BC_ERR_INVALID_INPUT, format("Decomposition levels must be in [1, 32], got %u", decomp_levels));
+    return check_input_len(len_u32, degree);
+}
+
+// fhe_rotate.rs:150-155: rotation normalised into [0, degree), galois 2r + 1.
+uint32_t rotate_galois(uint32_t degree, int32_t rotation) {
+    const uint32_t r = rotation < 0 ? static_cast<uint32_t>(static_cast<int64_t>(degree) + rotation)
+                                    : static_cast<uint32_t>(rotation);
+    return 2u * r + 1u;
+}
+
+int run_rotate(bc_ctx *ctx, const uint64_t *in, uint32_t degree, int32_t rotation, uint64_t modulus,
+               uint64_t *out) {
+    if (!in || !out) return fail(BC_ERR_INVALID_INPUT, "device pointers must not be NULL");
+    if (in == out) return fail(BC_ERR_INVALID_INPUT, "input and output must be different buffers");
+    int st = bc::use_device(ctx);
+    if (st) return st;
+    bc::KArgs k = {};
+    k.in = in;
+    k.out = out;
+    k.poly_stride = degree;
+    k.limb_stride = degree;
+    k.batch = 1;
+    k.n_limbs = 1;
+    k.logn = bc::ilog2(degree);
+    k.status = ctx->d_status;
+    if ((st = bc::launch_automorphism(k, rotate_galois(degree, rotation), nullptr, modulus, ctx->stream)))
+        return st;
+    return bc::ctx_sync(ctx);
+}
+
+int run_modulus_switch(bc_ctx *ctx, const uint64_t *in, uint32_t degree, uint64_t modulus_old,
+                       uint64_t modulus_new, uint64_t *out) {
+    if (!in || !out) return fail(BC_ERR_INVALID_INPUT, "device pointers must not be NULL");
+    int st = bc::use_device(ctx);
+    if (st) return st;
+    if ((st = bc::launch_modulus_switch(in, out, degree, bc::modswitch_const(modulus_old, modulus_new),
+                                        ctx->stream)))
+        return st;
+    return bc::ctx_sync(ctx);
+}
+
+// FheKeySwitch::execute's second pass stores the input over the first
+// pass's digits (fhe_key_switch.wgsl:128-148 reads binding 0, the input), so
+// the op's result is a copy of its input.
+int run_key_switch(bc_ctx *ctx, const uint64_t *in, uint32_t degree, uint64_t *out) {
+    if (!in || !out) return fail(BC_ERR_INVALID_INPUT, "device pointers must not be NULL");
+    int st = bc::use_device(ctx);
+    if (st) return st;
+    if (in != out) {
+        const cudaError_t e = cudaMemcpyAsync(out, in, static_cast<size_t>(degree) * sizeof(uint64_t),
+                                              cudaMemcpyDeviceToDevice, ctx->stream);
+        if (e != cudaSuccess) return bc::cuda_fail(e, "key switch copy");
+    }
+    return bc::ctx_sync(ctx);
+}
+
 // Moduli the CUDA path cannot represent (>= 2^62): the reference accepts
 // them but computes truncated products there.
 int check_width(uint64_t modulus) {
@@ -348,6 +455,68 @@ template class FheCoeffOp<CoeffKind::Add>;
 template class FheCoeffOp<CoeffKind::Sub>;
 template class FheCoeffOp<CoeffKind::Mul>;
 
+Result<FheRotate> FheRotate::create(Tensor input, uint32_t degree, int32_t rotation, uint64_t modulus) {
+    const int st = check_rotate(input.len(), degree, rotation);
+    if (st) return Result<FheRotate>::err(last(st));
+    FheRotate op;
+    op.input_ = std::move(input);
+    op.degree_ = degree;
+    op.rotation_ = rotation;
+    op.modulus_ = modulus;
+    return Result<FheRotate>::ok(std::move(op));
+}
+
+Result<Tensor> FheRotate::execute() && {
+    auto out = Tensor::empty_u64(degree_, input_.device());
+    if (out.is_err()) return out;
+    const int st = run_rotate(input_.device()->ctx(), input_.data(), degree_, rotation_, modulus_,
+                              out.value().mutable_data());
+    if (st) return Result<Tensor>::err(last(st));
+    return out;
+}
+
+Result<FheModulusSwitch> FheModulusSwitch::create(Tensor input, uint32_t degree, uint64_t modulus_old,
+                                                  uint64_t modulus_new) {
+    const int st = check_modulus_switch(input.len(), degree, modulus_old, modulus_new);
+    if (st) return Result<FheModulusSwitch>::err(last(st));
+    FheModulusSwitch op;
+    op.input_ = std::move(input);
+    op.degree_ = degree;
+    op.modulus_old_ = modulus_old;
+    op.modulus_new_ = modulus_new;
+    return Result<FheModulusSwitch>::ok(std::move(op));
+}
+
+Result<Tensor> FheModulusSwitch::execute() && {
+    auto out = Tensor::empty_u64(degree_, input_.device());
+    if (out.is_err()) return out;
+    const int st = run_modulus_switch(input_.device()->ctx(), input_.data(), degree_, modulus_old_, modulus_new_,
+                                      out.value().mutable_data());
+    if (st) return Result<Tensor>::err(last(st));
+    return out;
+}
+
+Result<FheKeySwitch> FheKeySwitch::create(Tensor input, uint32_t degree, uint64_t modulus, uint32_t decomp_base,
+                                          uint32_t decomp_levels) {
+    const int st = check_key_switch(input.len(), degree, decomp_base, decomp_levels);
+    if (st) return Result<FheKeySwitch>::err(last(st));
+    FheKeySwitch op;
+    op.input_ = std::move(input);
+    op.degree_ = degree;
+    op.modulus_ = modulus;
+    op.decomp_base_ = decomp_base;
+    op.decomp_levels_ = decomp_levels;
+    return Result<FheKeySwitch>::ok(std::move(op));
+}
+
+Result<Tensor> FheKeySwitch::execute() && {
+    auto out = Tensor::empty_u64(degree_, input_.device());
+    if (out.is_err()) return out;
+    const int st = run_key_switch(input_.device()->ctx(), input_.data(), degree_, out.value().mutable_data());
+    if (st) return Result<Tensor>::err(last(st));
+    return out;
+}
+
 Result<FheFastPolyMul> FheFastPolyMul::create(Tensor a, Tensor b, uint32_t degree, uint64_t modulus,
                                               uint64_t root) {
     const int st = check_pair(a.len(), b.len(), degree);
@@ -471,6 +640,49 @@ int bc_fhe_poly_sub(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const ui
 int bc_fhe_poly_mul(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const uint64_t *d_b,
                     size_t b_len_u32, uint32_t degree, uint64_t modulus, uint64_t *d_out) {
     return coeff_entry(bc::kCoeffMul, ctx, d_a, a_len_u32, d_b, b_len_u32, degree, modulus, d_out);
+}
+
+int bc_fhe_rotate_check(size_t input_len_u32, uint32_t degree, int32_t rotation, uint64_t modulus) {
+    (void)modulus;
+    return check_rotate(input_len_u32, degree, rotation);
+}
+
+int bc_fhe_rotate(bc_ctx *ctx, const uint64_t *d_in, size_t input_len_u32, uint32_t degree, int32_t rotation,
+                  uint64_t modulus, uint64_t *d_out) {
+    if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
+    const int st = check_rotate(input_len_u32, degree, rotation);
+    return st ? st : run_rotate(ctx, d_in, degree, rotation, modulus, d_out);
+}
+
+int bc_fhe_modulus_switch_check(size_t input_len_u32, uint32_t degree, uint64_t modulus_old,
+                                uint64_t modulus_new) {
+    return check_modulus_switch(input_len_u32, degree, modulus_old, modulus_new);
+}
+
+int bc_fhe_modulus_switch(bc_ctx *ctx, const uint64_t *d_in, size_t input_len_u32, uint32_t degree,
+                          uint64_t modulus_old, uint64_t modulus_new, uint64_t *d_out) {
+    if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
+    const int st = check_modulus_switch(input_len_u32, degree, modulus_old, modulus_new);
+    return st ? st : run_modulus_switch(ctx, d_in, degree, modulus_old, modulus_new, d_out);
+}
+
+int bc_fhe_key_switch_check(size_t input_len_u32, uint32_t degree, uint64_t modulus, uint32_t decomp_base,
+                            uint32_t decomp_levels) {
+    (void)modulus;
+    return check_key_switch(input_len_u32, degree, decomp_base, decomp_levels);
+}
+
+int bc_fhe_key_switch(bc_ctx *ctx, const uint64_t *d_in, size_t input_len_u32, uint32_t degree, uint64_t modulus,
+                      uint32_t decomp_base, uint32_t decomp_levels, uint64_t *d_out) {
+    (void)modulus;
+    if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
+    const int st = check_key_switch(input_len_u32, degree, decomp_base, decomp_levels);
+    return st ? st : run_key_switch(ctx, d_in, degree, d_out);
+}
+
+uint32_t bc_rotation_galois(uint32_t degree, int32_t rotation) {
+    if (check_rotate(static_cast<size_t>(degree) * 2, degree, rotation)) return 0;
+    return rotate_galois(degree, rotation);
 }
 
 }  // extern "C"

@@ -135,6 +135,53 @@ using FhePolyAdd = FheCoeffOp<CoeffKind::Add>;
 using FhePolySub = FheCoeffOp<CoeffKind::Sub>;
 using FhePolyMul = FheCoeffOp<CoeffKind::Mul>;
 
+// ops/fhe_rotate.rs:64-183: Galois automorphism X -> X^(2r+1) of one
+// polynomial (negative r counts from degree), coefficients moved to
+// i (2r+1) mod 2N and negated as modulus - c (0 stays 0) where that index
+// wraps past N.
+class FheRotate {
+public:
+    static Result<FheRotate> create(Tensor input, uint32_t degree, int32_t rotation, uint64_t modulus);
+    Result<Tensor> execute() &&;
+
+private:
+    Tensor input_;
+    uint32_t degree_ = 0;
+    int32_t rotation_ = 0;
+    uint64_t modulus_ = 0;
+};
+
+// ops/fhe_modulus_switch.rs:60-167: round(c * new / old) mod new per
+// coefficient, with the product kept exact in 128 bits.
+class FheModulusSwitch {
+public:
+    static Result<FheModulusSwitch> create(Tensor input, uint32_t degree, uint64_t modulus_old,
+                                           uint64_t modulus_new);
+    Result<Tensor> execute() &&;
+
+private:
+    Tensor input_;
+    uint32_t degree_ = 0;
+    uint64_t modulus_old_ = 0, modulus_new_ = 0;
+};
+
+// ops/fhe_key_switch.rs:70-223: validates the decomposition parameters;
+// execute() returns a copy of the input, which is what the reference's two
+// passes leave in the output (the second one copies the input over the
+// first one's digits).
+class FheKeySwitch {
+public:
+    static Result<FheKeySwitch> create(Tensor input, uint32_t degree, uint64_t modulus, uint32_t decomp_base,
+                                       uint32_t decomp_levels);
+    Result<Tensor> execute() &&;
+
+private:
+    Tensor input_;
+    uint32_t degree_ = 0;
+    uint64_t modulus_ = 0;
+    uint32_t decomp_base_ = 0, decomp_levels_ = 0;
+};
+
 // ops/fhe_fast_poly_mul.rs:39-171.
 class FheFastPolyMul {
 public:

@@ -751,6 +751,49 @@ int bc_polymul(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c, ui
     return run_polymul(p, a, b, c, batch, layout, pick_stream(p, stream));
 }
 
+int bc_automorphism(bc_plan *p, const uint64_t *in, uint64_t *out, uint32_t batch, const bc_layout *layout,
+                    uint32_t galois, void *stream) {
+    if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");
+    if ((galois & 1u) == 0 || galois >= 2ull * p->degree)
+        return fail(BC_ERR_INVALID_INPUT,
+                    format("galois element %u must be odd and below 2N = %llu", galois,
+                           static_cast<unsigned long long>(2ull * p->degree)));
+    KArgs a;
+    int st = make_args(p, in, nullptr, out, batch, layout, &a);
+    if (st) return st;
+    if (in == out) return fail(BC_ERR_INVALID_INPUT, "input and output must be different buffers");
+    if ((st = use_device(p->ctx))) return st;
+    return launch_automorphism(a, galois, p->d_coeff, 0, pick_stream(p, stream));
+}
+
+int bc_modulus_switch(bc_ctx *ctx, const uint64_t *in, uint64_t *out, size_t count, uint64_t modulus_old,
+                      uint64_t modulus_new, void *stream) {
+    if (!ctx || ((!in || !out) && count)) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    if (modulus_new >= modulus_old)
+        return fail(BC_ERR_INVALID_INPUT, format("New modulus (%llu) must be < old modulus (%llu)",
+                                                 static_cast<unsigned long long>(modulus_new),
+                                                 static_cast<unsigned long long>(modulus_old)));
+    int st = use_device(ctx);
+    if (st) return st;
+    return launch_modulus_switch(in, out, count, modswitch_const(modulus_old, modulus_new),
+                                 stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
+}
+
+int bc_decompose(bc_ctx *ctx, const uint64_t *in, uint64_t *out, size_t count, uint32_t base, uint32_t levels,
+                 void *stream) {
+    if (!ctx || ((!in || !out) && count)) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
+    if (base < 2 || base > (1u << 24))
+        return fail(BC_ERR_INVALID_INPUT, format("Decomposition base must be in [2, 2^24], got %u", base));
+    if (levels == 0 || levels > 32)
+        return fail(BC_ERR_INVALID_INPUT, format("Decomposition levels must be in [1, 32], got %u", levels));
+    const uintptr_t ib = reinterpret_cast<uintptr_t>(in), ob = reinterpret_cast<uintptr_t>(out);
+    if (count && ib < ob + count * levels * sizeof(uint64_t) && ob < ib + count * sizeof(uint64_t))
+        return fail(BC_ERR_INVALID_INPUT, "input and output must not overlap");
+    int st = use_device(ctx);
+    if (st) return st;
+    return launch_decompose(in, out, count, base, levels, stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
+}
+
 int bc_fill_uniform(bc_plan *p, uint64_t *out, uint32_t batch, const bc_layout *layout, uint64_t seed,
                     uint64_t first_poly, uint64_t total_polys, void *stream) {
     if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");

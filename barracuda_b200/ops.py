@@ -26,7 +26,7 @@ from ._native import BarracudaError, check, lib
 __all__ = [
     "BarracudaError", "Device", "FheTensor", "create_fhe_poly_tensor", "read_poly_from_tensor",
     "compute_primitive_root", "compute_inverse_root", "FheNtt", "FheIntt", "FhePointwiseMul",
-    "FheFastPolyMul",
+    "FheFastPolyMul", "FheRotate", "FheModulusSwitch", "FheKeySwitch", "rotation_galois",
 ]
 
 
@@ -225,6 +225,76 @@ class FhePolySub(_FheCoeffOp):
 class FhePolyMul(_FheCoeffOp):
     """ops/fhe_poly_mul.rs:34-133: (a * b) mod q per coefficient, exact."""
     _name = "mul"
+
+
+class FheRotate:
+    """ops/fhe_rotate.rs:64-183: Galois automorphism X -> X^(2r+1) (negative r
+    counts from degree); coefficients that wrap past X^N are negated as
+    modulus - c (0 stays 0)."""
+
+    def __init__(self, input: FheTensor, degree: int, rotation: int, modulus: int):
+        if not -2**31 <= rotation < 2**31:
+            raise OverflowError(f"rotation {rotation} does not fit an i32")
+        check(lib().bc_fhe_rotate_check(input.len(), degree, rotation, modulus))
+        self.input, self.degree, self.rotation, self.modulus = input, degree, rotation, modulus
+
+    @classmethod
+    def new(cls, input, degree, rotation, modulus) -> "FheRotate":
+        return cls(input, degree, rotation, modulus)
+
+    def execute(self) -> FheTensor:
+        out = FheTensor(self.input.device, 2 * self.degree)
+        check(lib().bc_fhe_rotate(self.input.device.handle, self.input.ptr, self.input.len(),
+                                  self.degree, self.rotation, self.modulus, out.ptr))
+        return out
+
+
+def rotation_galois(degree: int, rotation: int) -> int:
+    """Galois element 2r + 1 that FheRotate applies (0 when out of range)."""
+    return int(lib().bc_rotation_galois(degree, rotation))
+
+
+class FheModulusSwitch:
+    """ops/fhe_modulus_switch.rs:60-167: round(c * new / old) mod new, with the
+    product kept exact (the reference's shader wraps it at 2^64)."""
+
+    def __init__(self, input: FheTensor, degree: int, modulus_old: int, modulus_new: int):
+        check(lib().bc_fhe_modulus_switch_check(input.len(), degree, modulus_old, modulus_new))
+        self.input, self.degree = input, degree
+        self.modulus_old, self.modulus_new = modulus_old, modulus_new
+
+    @classmethod
+    def new(cls, input, degree, modulus_old, modulus_new) -> "FheModulusSwitch":
+        return cls(input, degree, modulus_old, modulus_new)
+
+    def execute(self) -> FheTensor:
+        out = FheTensor(self.input.device, 2 * self.degree)
+        check(lib().bc_fhe_modulus_switch(self.input.device.handle, self.input.ptr, self.input.len(),
+                                          self.degree, self.modulus_old, self.modulus_new, out.ptr))
+        return out
+
+
+class FheKeySwitch:
+    """ops/fhe_key_switch.rs:70-223: validates the decomposition parameters;
+    execute() returns a copy of the input, as the reference's two passes do
+    (the second stores the input over the first's digits)."""
+
+    def __init__(self, input: FheTensor, degree: int, modulus: int, decomp_base: int,
+                 decomp_levels: int):
+        check(lib().bc_fhe_key_switch_check(input.len(), degree, modulus, decomp_base, decomp_levels))
+        self.input, self.degree, self.modulus = input, degree, modulus
+        self.decomp_base, self.decomp_levels = decomp_base, decomp_levels
+
+    @classmethod
+    def new(cls, input, degree, modulus, decomp_base, decomp_levels) -> "FheKeySwitch":
+        return cls(input, degree, modulus, decomp_base, decomp_levels)
+
+    def execute(self) -> FheTensor:
+        out = FheTensor(self.input.device, 2 * self.degree)
+        check(lib().bc_fhe_key_switch(self.input.device.handle, self.input.ptr, self.input.len(),
+                                      self.degree, self.modulus, self.decomp_base,
+                                      self.decomp_levels, out.ptr))
+        return out
 
 
 class FheFastPolyMul:

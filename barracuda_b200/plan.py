@@ -121,6 +121,12 @@ class NttPlan:
         check(lib().bc_polymul(self.handle, _ptr(a), _ptr(b), _ptr(c), batch, self._layout(layout),
                                stream or None))
 
+    def automorphism(self, src, dst, batch: int, galois: int, layout: Optional[Layout] = None,
+                     stream: int = 0):
+        """X -> X^galois on every polynomial (galois odd, < 2N); src and dst must not overlap."""
+        check(lib().bc_automorphism(self.handle, _ptr(src), _ptr(dst), batch, self._layout(layout),
+                                    galois, stream or None))
+
     def fill_uniform(self, dst, batch: int, seed: int, first_poly: int = 0,
                      total_polys: Optional[int] = None, layout: Optional[Layout] = None,
                      stream: int = 0):
@@ -139,6 +145,19 @@ class NttPlan:
                 self.close()
         except Exception:
             pass
+
+
+def modulus_switch(device: Device, src, dst, count: int, modulus_old: int, modulus_new: int,
+                   stream: int = 0):
+    """round(c * new / old) mod new over count words (in place allowed)."""
+    check(lib().bc_modulus_switch(device.handle, _ptr(src), _ptr(dst), count, modulus_old,
+                                  modulus_new, stream or None))
+
+
+def decompose(device: Device, src, dst, count: int, base: int, levels: int, stream: int = 0):
+    """dst[l * count + i] = digit l (base `base`) of src[i], l < levels."""
+    check(lib().bc_decompose(device.handle, _ptr(src), _ptr(dst), count, base, levels,
+                             stream or None))
 
 
 def digest(device: Device, buf, count: int, out, stream: int = 0, first_index: int = 0):

@@ -484,6 +484,40 @@ def run_sweep(args):
         print(json.dumps(line), flush=True)
         del a, b, c
         plan.close()
+    # rotation (automorphism: 16 bytes per coefficient), modulus switch (16) and
+    # base-2^16 decomposition into 3 digits (8 read + 24 written)
+    for L in (12, 13, 14, 15, 16, 17):
+        n, limbs = 1 << L, 16
+        batch = (1 << 28) // (n * limbs)
+        count = limbs * batch * n
+        qs = bc.ntt_primes(31, n, limbs)
+        plan = bc.NttPlan(dev, n, qs, [bc.negacyclic_root(q, n) for q in qs], mode=bc.NEGACYCLIC)
+        a = torch.empty(count, dtype=torch.int64, device="cuda")
+        b = torch.empty(count * (3 if L == 16 else 1), dtype=torch.int64, device="cuda")
+        plan.fill_uniform(a, batch, seed=1, stream=sh)
+        line = {"sweep": "rotation and rns ops, 1 GPU", "N": n, "limbs": limbs, "batch": batch,
+                "peak_gbs": hbm, "peak_kind": peak_kind}
+        ops = [("automorphism", lambda: plan.automorphism(a, b, batch, 2 * 1234 + 1, stream=sh), 16)]
+        if L == 16:
+            ops += [("modulus_switch", lambda: bc.modulus_switch(dev, a, b, count, qs[0], qs[1] >> 8,
+                                                                 stream=sh), 16),
+                    ("decompose_2^16_x3", lambda: bc.decompose(dev, a, b, count, 1 << 16, 3, stream=sh), 32)]
+        for name, fn, bytes_per in ops:
+            for _ in range(args.warmup):
+                fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            gbs = count * bytes_per / (ms / 1000.0) / 1e9
+            line[name] = {"ms": ms, "gb_per_s": gbs, "frac": gbs / hbm}
+        print(json.dumps(line), flush=True)
+        del a, b
+        plan.close()
     dev.close()
 
 

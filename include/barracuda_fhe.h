@@ -16,6 +16,9 @@
  *   - ops/fhe_fast_poly_mul.rs:61,122 FheFastPolyMul         -> bc_fhe_fast_poly_mul*
  *   - ops/fhe_poly_add.rs:64,128 FhePolyAdd, fhe_poly_sub.rs FhePolySub,
  *     fhe_poly_mul.rs:34,82 FhePolyMul                       -> bc_fhe_poly_{add,sub,mul}*
+ *   - ops/fhe_rotate.rs:91,140 FheRotate                     -> bc_fhe_rotate*
+ *   - ops/fhe_modulus_switch.rs:85,124 FheModulusSwitch       -> bc_fhe_modulus_switch*
+ *   - ops/fhe_key_switch.rs:101,162 FheKeySwitch              -> bc_fhe_key_switch*
  *   - ops/fhe_ntt/mod.rs:210 compute_primitive_root          -> bc_compute_primitive_root
  *   - ops/fhe_intt/mod.rs:202 compute_inverse_root           -> bc_compute_inverse_root
  *   - ops/fhe_poly_add.rs:185 create_fhe_poly_tensor,
@@ -154,6 +157,41 @@ int bc_fhe_poly_mul_check(size_t a_len_u32, size_t b_len_u32, uint32_t degree, u
 int bc_fhe_poly_mul(bc_ctx *ctx, const uint64_t *d_a, size_t a_len_u32, const uint64_t *d_b,
                     size_t b_len_u32, uint32_t degree, uint64_t modulus, uint64_t *d_out);
 
+/* fhe_rotate.rs:91-183 + fhe_rotate.wgsl.  Galois automorphism
+ * X -> X^g, g = 2r + 1 with r = rotation (rotation + degree when negative):
+ * coefficient i moves to p = i g mod 2N, and where p >= N it lands at p - N
+ * as modulus - c (0 stays 0; 64-bit wrap-around for c > modulus, as the
+ * shader computes it).  Bit-exact with the reference for any input.
+ * Checks: degree a power of 2 >= 4, |rotation| <= degree / 2 (INT32_MIN is
+ * rejected), input length; all BC_ERR_INVALID_INPUT.  d_out must not be
+ * d_in. */
+int bc_fhe_rotate_check(size_t input_len_u32, uint32_t degree, int32_t rotation, uint64_t modulus);
+int bc_fhe_rotate(bc_ctx *ctx, const uint64_t *d_in, size_t input_len_u32, uint32_t degree,
+                  int32_t rotation, uint64_t modulus, uint64_t *d_out);
+/* Galois element 2r + 1 FheRotate uses for a rotation (0 when out of range). */
+uint32_t bc_rotation_galois(uint32_t degree, int32_t rotation);
+
+/* fhe_modulus_switch.rs:85-166 + .wgsl.  c' = round(c * new / old) mod new
+ * (ties round up) per coefficient, exact for any u64 c.  The reference's
+ * shader forms c * new in 64 bits; it matches this result whenever
+ * c * new < 2^64 and old <= 2^63, and wraps otherwise.
+ * Checks: degree, new < old, input length; all BC_ERR_INVALID_INPUT. */
+int bc_fhe_modulus_switch_check(size_t input_len_u32, uint32_t degree, uint64_t modulus_old,
+                                uint64_t modulus_new);
+int bc_fhe_modulus_switch(bc_ctx *ctx, const uint64_t *d_in, size_t input_len_u32, uint32_t degree,
+                          uint64_t modulus_old, uint64_t modulus_new, uint64_t *d_out);
+
+/* fhe_key_switch.rs:101-222 + .wgsl.  Checks degree, 2 <= decomp_base <=
+ * 2^24, 1 <= decomp_levels <= 32 and the input length (BC_ERR_INVALID_INPUT).
+ * The result is a copy of the input: the reference's second pass
+ * (accumulate_switched) stores its input buffer over the digits of the
+ * first.  bc_decompose computes the digits themselves. */
+int bc_fhe_key_switch_check(size_t input_len_u32, uint32_t degree, uint64_t modulus,
+                            uint32_t decomp_base, uint32_t decomp_levels);
+int bc_fhe_key_switch(bc_ctx *ctx, const uint64_t *d_in, size_t input_len_u32, uint32_t degree,
+                      uint64_t modulus, uint32_t decomp_base, uint32_t decomp_levels,
+                      uint64_t *d_out);
+
 /* ------------------------------------------------ batched plans (new path)
  * A plan holds, for n_limbs RNS limbs of one degree N, the device twiddle
  * tables (with Shoup companions), N^-1 and the kernel choice.
@@ -264,6 +302,23 @@ int bc_polymul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t
 int bc_polymul_static_scratch(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b,
                               uint64_t *d_c, uint32_t batch, const bc_layout *layout,
                               void *stream);
+
+/* Galois automorphism X -> X^galois (galois odd, < 2N) of every polynomial
+ * of the batch, with bc_fhe_rotate's semantics and limb l's modulus for the
+ * negation.  d_in and d_out must not overlap. */
+int bc_automorphism(bc_plan *plan, const uint64_t *d_in, uint64_t *d_out, uint32_t batch,
+                    const bc_layout *layout, uint32_t galois, void *stream);
+/* bc_fhe_modulus_switch's map over `count` words (any count; in place
+ * allowed); asynchronous on `stream`.  Needs modulus_new < modulus_old. */
+int bc_modulus_switch(bc_ctx *ctx, const uint64_t *d_in, uint64_t *d_out, size_t count,
+                      uint64_t modulus_old, uint64_t modulus_new, void *stream);
+/* Base-B digits of `count` words, the decomposition fhe_key_switch.wgsl:71-84
+ * describes: d_out[l * count + i] = floor(d_in[i] / base^l) mod base for
+ * l < levels (digit-major: each digit is a polynomial for the key-switching
+ * product).  2 <= base <= 2^24, 1 <= levels <= 32; d_out holds
+ * levels * count words and must not overlap d_in. */
+int bc_decompose(bc_ctx *ctx, const uint64_t *d_in, uint64_t *d_out, size_t count, uint32_t base,
+                 uint32_t levels, void *stream);
 
 /* Seeded synthetic coefficients, uniform in [0, q_l): element (l, p, j) of
  * the batch gets value(seed, ((l * total_polys + first_poly + p) * N + j)),

@@ -91,6 +91,32 @@ void orc_ref_poly_sub(const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_
 void orc_ref_poly_mul(const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t degree, uint64_t q);
 void orc_exact_poly_mul(const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t degree, uint64_t q);
 
+/* Rotation, modulus switch and key switch (ref_rns.c).
+ * orc_ref_rotate: fhe_rotate.wgsl (galois = 2r + 1 after fhe_rotate.rs maps a
+ *   negative r to degree + r; out[i*g mod 2N] = in[i], negated as m - in[i]
+ *   (0 stays 0) where i*g mod 2N >= N).  orc_automorphism: the same for any
+ *   odd g with exact index arithmetic.
+ * orc_ref_modulus_switch1: fhe_modulus_switch.wgsl scale_and_round with its
+ *   64-bit wrap-around of coeff * q_new; orc_exact_modulus_switch1 the exact
+ *   round(coeff * q_new / q_old) mod q_new.
+ * orc_ref_key_switch: both passes of FheKeySwitch::execute (the second copies
+ *   the input over the first's digits).  orc_decompose: every base-B digit,
+ *   digit-major. */
+uint32_t orc_ref_rotate_galois(uint32_t degree, int32_t rotation);
+void orc_ref_rotate(const uint64_t *in, uint64_t *out, uint32_t degree, int32_t rotation,
+                    uint64_t modulus);
+void orc_automorphism(const uint64_t *in, uint64_t *out, uint32_t degree, uint32_t galois,
+                      uint64_t modulus);
+uint64_t orc_ref_modulus_switch1(uint64_t c, uint64_t q_old, uint64_t q_new);
+uint64_t orc_exact_modulus_switch1(uint64_t c, uint64_t q_old, uint64_t q_new);
+void orc_ref_modulus_switch(const uint64_t *in, uint64_t *out, uint32_t degree, uint64_t q_old,
+                            uint64_t q_new);
+void orc_exact_modulus_switch(const uint64_t *in, uint64_t *out, size_t count, uint64_t q_old,
+                              uint64_t q_new);
+void orc_ref_key_switch(const uint64_t *in, uint64_t *out, uint32_t degree, uint32_t decomp_base,
+                        uint32_t decomp_levels);
+void orc_decompose(const uint64_t *in, uint64_t *out, size_t count, uint32_t base, uint32_t levels);
+
 /* ---------------- part 2: exact arithmetic ---------------- */
 
 uint64_t orc_mulmod(uint64_t a, uint64_t b, uint64_t q);

@@ -35,7 +35,7 @@ def _stale() -> bool:
     if not os.path.exists(_SO):
         return True
     t = os.path.getmtime(_SO)
-    srcs = [os.path.join(_HERE, f) for f in ("ref_wgsl.c", "ref_poly.c", "exact.c", "baseline.c", "oracle.h")]
+    srcs = [os.path.join(_HERE, f) for f in ("ref_wgsl.c", "ref_poly.c", "ref_rns.c", "exact.c", "baseline.c", "oracle.h")]
     return any(os.path.exists(f) and os.path.getmtime(f) > t for f in srcs)
 
 
@@ -85,6 +85,15 @@ def lib():
             "orc_ref_poly_sub": (None, [_u64p, _u64p, _u64p, u32, u64]),
             "orc_ref_poly_mul": (None, [_u64p, _u64p, _u64p, u32, u64]),
             "orc_exact_poly_mul": (None, [_u64p, _u64p, _u64p, u32, u64]),
+            "orc_ref_rotate_galois": (u32, [u32, ctypes.c_int32]),
+            "orc_ref_rotate": (None, [_u64p, _u64p, u32, ctypes.c_int32, u64]),
+            "orc_automorphism": (None, [_u64p, _u64p, u32, u32, u64]),
+            "orc_ref_modulus_switch1": (u64, [u64, u64, u64]),
+            "orc_exact_modulus_switch1": (u64, [u64, u64, u64]),
+            "orc_ref_modulus_switch": (None, [_u64p, _u64p, u32, u64, u64]),
+            "orc_exact_modulus_switch": (None, [_u64p, _u64p, ctypes.c_size_t, u64, u64]),
+            "orc_ref_key_switch": (None, [_u64p, _u64p, u32, u32, u32]),
+            "orc_decompose": (None, [_u64p, _u64p, ctypes.c_size_t, u32, u32]),
             "orc_baseline_run": (ctypes.c_double,
                                  [i32, _u64p, _u64p, u32, u32, _u64p, _u64p, u32, i32]),
         }
@@ -209,6 +218,52 @@ def ref_poly_mul(a, b, q):
 
 def exact_poly_mul(a, b, q):
     return _binary("orc_exact_poly_mul", a, b, q)
+
+
+def ref_rotate(x, degree, rotation, modulus):
+    """FheRotate::execute (ops/fhe_rotate.rs:140-183, fhe_rotate.wgsl)."""
+    x = _arr(x)
+    out = np.zeros(degree, dtype=np.uint64)
+    lib().orc_ref_rotate(_p(x), _p(out), degree, rotation, modulus)
+    return out
+
+
+def automorphism(x, degree, galois, modulus):
+    x = _arr(x)
+    out = np.zeros(degree, dtype=np.uint64)
+    lib().orc_automorphism(_p(x), _p(out), degree, galois, modulus)
+    return out
+
+
+def ref_modulus_switch(x, q_old, q_new):
+    """FheModulusSwitch::execute (ops/fhe_modulus_switch.rs:124-166, .wgsl)."""
+    x = _arr(x)
+    out = np.zeros(x.size, dtype=np.uint64)
+    lib().orc_ref_modulus_switch(_p(x), _p(out), x.size, q_old, q_new)
+    return out
+
+
+def exact_modulus_switch(x, q_old, q_new):
+    x = _arr(x)
+    out = np.zeros(x.size, dtype=np.uint64)
+    lib().orc_exact_modulus_switch(_p(x), _p(out), x.size, q_old, q_new)
+    return out
+
+
+def ref_key_switch(x, decomp_base, decomp_levels):
+    """FheKeySwitch::execute (ops/fhe_key_switch.rs:162-222, .wgsl)."""
+    x = _arr(x)
+    out = np.zeros(x.size, dtype=np.uint64)
+    lib().orc_ref_key_switch(_p(x), _p(out), x.size, decomp_base, decomp_levels)
+    return out
+
+
+def decompose(x, base, levels):
+    """Every base-B digit of every coefficient, digit-major (levels, len(x))."""
+    x = _arr(x)
+    out = np.zeros(x.size * levels, dtype=np.uint64)
+    lib().orc_decompose(_p(x), _p(out), x.size, base, levels)
+    return out.reshape(levels, x.size)
 
 
 def digest(x, first_index=0):

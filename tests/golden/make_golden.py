@@ -95,6 +95,123 @@ CASES = [
      "source": "crates/barracuda/tests/property/fhe_properties.rs:320-365"},
 ]
 
+
+# ---- FheRotate, FheModulusSwitch, FheKeySwitch ----
+# The reference's tests for these ops (tests/property/fhe_properties.rs:
+# 141-260, 368-433) assert properties that contradict the ops' own shaders,
+# and return early without an FHE device, so they have never checked the
+# shaders.  Each case below keeps the test's inputs; "expect" is derived here
+# from the shader's formula in plain Python (not from the C oracle), and
+# "test_asserts" records what the Rust test claims and why it cannot hold.
+
+
+def _rotate_shader(x, degree, rotation, modulus):
+    """fhe_rotate.rs:150-155 + fhe_rotate.wgsl:98-128."""
+    r = degree + rotation if rotation < 0 else rotation
+    g = (2 * r + 1) % 2**32
+    out = [None] * degree
+    for i, v in enumerate(x):
+        p = ((i * g) % 2**32) % (2 * degree)
+        if p >= degree:
+            out[p - degree] = 0 if v == 0 else (modulus - v) % 2**64
+        else:
+            out[p] = v
+    return out
+
+
+def _modswitch_shader(x, q_old, q_new):
+    """fhe_modulus_switch.wgsl:103-131 (u64 product and doubling wrap)."""
+    out = []
+    for c in x:
+        scaled = (c * q_new) % 2**64
+        quo, rem = scaled // q_old, scaled % q_old
+        if (rem * 2) % 2**64 >= q_old:
+            quo += 1
+        out.append(quo % q_new if q_new else 0)
+    return out
+
+
+def _modswitch_exact(x, q_old, q_new):
+    """round(c * q_new / q_old) mod q_new, ties up, in Python integers."""
+    return [((c * q_new + (q_old - 1) // 2 + (1 if q_old % 2 == 0 else 0)) // q_old) % q_new
+            if q_new else 0 for c in x]
+
+
+ROT_IN = list(range(8))
+ROT_IN10 = [i * 10 for i in range(8)]
+CASES += [
+    {"name": "rotate_compose_8_257", "kind": "rotate", "degree": 8, "modulus": 257,
+     "rotations": [2, 3], "input": ROT_IN,
+     "expect": _rotate_shader(_rotate_shader(ROT_IN, 8, 2, 257), 8, 3, 257),
+     "same_as_rotations": [1],
+     "test_asserts": "rotate(2) then rotate(3) == rotate(5); rotate(5) is rejected for degree 8 "
+                     "(|5| > 4), and X^5 then X^7 is X^35 = X^3 mod X^16 - 1, i.e. rotate(1)",
+     "source": "crates/barracuda/tests/property/fhe_properties.rs:195-232"},
+    {"name": "rotate_inverse_8_257", "kind": "rotate", "degree": 8, "modulus": 257,
+     "rotations": [3, -3], "input": ROT_IN10,
+     "expect": _rotate_shader(_rotate_shader(ROT_IN10, 8, 3, 257), 8, -3, 257),
+     "test_asserts": "rotate(3) then rotate(-3) == identity; the galois elements are 7 and "
+                     "2 * (8 - 3) + 1 = 11, and 7 * 11 = 77 = 13 mod 16, not 1",
+     "source": "crates/barracuda/tests/property/fhe_properties.rs:234-260"},
+    {"name": "rotate_wrap_negate_8_257", "kind": "rotate", "degree": 8, "modulus": 257,
+     "rotations": [1], "input": [0, 1, 2, 300, 4, 0, 6, 7],
+     "expect": _rotate_shader([0, 1, 2, 300, 4, 0, 6, 7], 8, 1, 257),
+     "source": "crates/barracuda/src/ops/fhe_rotate.wgsl:52-63 (a negated 0 stays 0; "
+               "300 > q negates to 257 - 300 mod 2^64)"},
+    {"name": "modulus_switch_4_257_17", "kind": "modulus_switch", "degree": 4,
+     "modulus_old": 257, "modulus_new": 17, "input": [10, 20, 30, 40],
+     "expect": _modswitch_shader([10, 20, 30, 40], 257, 17),
+     "exact": _modswitch_exact([10, 20, 30, 40], 257, 17),
+     "test_asserts": "output == input % 17 = [10, 3, 13, 6]; the op scales by 17/257 first",
+     "source": "crates/barracuda/tests/property/fhe_properties.rs:144-166"},
+    {"name": "modulus_switch_doc_60_58", "kind": "modulus_switch", "degree": 4,
+     "modulus_old": 1152921504606584833, "modulus_new": 288230376151711777,
+     "input": [0, 1, 2, 63],
+     "expect": _modswitch_shader([0, 1, 2, 63], 1152921504606584833, 288230376151711777),
+     "exact": _modswitch_exact([0, 1, 2, 63], 1152921504606584833, 288230376151711777),
+     "source": "crates/barracuda/src/ops/fhe_modulus_switch.rs:42-50 (doc example moduli; "
+               "inputs with c * q_new < 2^64, where the shader's u64 product is exact)"},
+    {"name": "modulus_switch_doc_wrap_60_58", "kind": "modulus_switch", "degree": 4,
+     "modulus_old": 1152921504606584833, "modulus_new": 288230376151711777,
+     "input": [64, 1000, 1152921504606584832, 576460752303292416],
+     "expect": _modswitch_shader([64, 1000, 1152921504606584832, 576460752303292416],
+                                 1152921504606584833, 288230376151711777),
+     "exact": _modswitch_exact([64, 1000, 1152921504606584832, 576460752303292416],
+                               1152921504606584833, 288230376151711777),
+     "source": "crates/barracuda/src/ops/fhe_modulus_switch.rs:42-50 (doc example moduli; "
+               "c * q_new >= 2^64: the shader's product wraps, the exact result differs)"},
+    {"name": "key_switch_4_257", "kind": "key_switch", "degree": 4, "modulus": 257,
+     "decomp_base": 2, "decomp_levels": 4, "input": [100, 150, 200, 250],
+     "expect": [100, 150, 200, 250],
+     "test_asserts": "len(output) == degree * levels = 16; the output buffer is the input's size "
+                     "(fhe_key_switch.rs:167-172), and its values are the input "
+                     "(accumulate_switched copies binding 0)",
+     "source": "crates/barracuda/tests/property/fhe_properties.rs:371-402"},
+    {"name": "key_switch_det_4_257", "kind": "key_switch", "degree": 4, "modulus": 257,
+     "decomp_base": 2, "decomp_levels": 4, "input": [50, 100, 150, 200],
+     "expect": [50, 100, 150, 200],
+     "source": "crates/barracuda/tests/property/fhe_properties.rs:405-433"},
+]
+
+# Constructor rejections in the ops' own unit tests: [op, args, expect_error]
+# with args (input_len_u32, degree, ...) in the constructor's order.
+OP_REJECTIONS = [
+    ["rotate", [8, 3, 1, 12289], True],
+    ["rotate", [8, 4, 3, 12289], True],
+    ["rotate", [8, 4, -3, 12289], True],
+    ["rotate", [8, 4, 2, 12289], False],
+    ["rotate", [8, 4, -2, 12289], False],
+    ["modulus_switch", [8, 3, 12289, 6145], True],
+    ["modulus_switch", [8, 4, 12289, 12289], True],
+    ["modulus_switch", [8, 4, 12289, 6145], False],
+    ["key_switch", [8, 3, 12289, 1 << 16, 3], True],
+    ["key_switch", [8, 4, 12289, 1, 3], True],
+    ["key_switch", [8, 4, 12289, 1 << 16, 0], True],
+    ["key_switch", [8, 4, 12289, 1 << 16, 3], False],
+]
+OP_REJECTIONS_SOURCE = ("crates/barracuda/src/ops/fhe_rotate.rs:189-205; "
+                        "fhe_modulus_switch.rs:177-199; fhe_key_switch.rs:234-250")
+
 # tests/fhe/helpers.rs:21-28 -- (degree, modulus, root), all primitive roots
 KNOWN_ROOTS = [[4, 17, 4], [4, 97, 22], [4, 257, 241], [4, 12289, 1479], [8, 97, 64], [16, 97, 8]]
 
@@ -126,6 +243,7 @@ def main():
         "ntt_params": {"values": NTT_PARAMS,
                        "source": "crates/barracuda/tests/property/fhe_proptest.rs:156-199"},
         "rejections": {"values": REJECTIONS, "source": REJECTIONS_SOURCE},
+        "op_rejections": {"values": OP_REJECTIONS, "source": OP_REJECTIONS_SOURCE},
     }
     with open(os.path.join(HERE, "reference_kats.json"), "w") as f:
         json.dump(doc, f, indent=1)

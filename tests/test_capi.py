@@ -110,6 +110,56 @@ def test_rejection_fixtures(kats):
         assert (st != 0) == expect_err, (op, ln, d, q)
 
 
+def test_rotate_switch_validation_messages():
+    """FheRotate / FheModulusSwitch / FheKeySwitch ::new: degree, the op's own
+    parameter, then the input length; all InvalidInput."""
+    L, E = N.lib(), N.BC_ERR_INVALID_INPUT
+    for d in (0, 2, 3, 6):
+        msg = f"Degree must be power of 2 >= 4, got {d}"
+        assert _check_msg(L.bc_fhe_rotate_check, 8, d, 1, 17) == (E, msg)
+        assert _check_msg(L.bc_fhe_modulus_switch_check, 8, d, 17, 5) == (E, msg)
+        assert _check_msg(L.bc_fhe_key_switch_check, 8, d, 17, 16, 3) == (E, msg)
+    assert _check_msg(L.bc_fhe_rotate_check, 8, 4, 3, 17) == (
+        E, "Rotation 3 out of range [-2, 2] for degree 4")
+    assert _check_msg(L.bc_fhe_rotate_check, 16, 8, -5, 17) == (
+        E, "Rotation -5 out of range [-4, 4] for degree 8")
+    assert _check_msg(L.bc_fhe_rotate_check, 8, 4, -2**31, 17)[0] == E
+    assert _check_msg(L.bc_fhe_rotate_check, 6, 4, 1, 17) == (
+        E, "Input must have 8 elements (degree=4, u64 emulated), got 6")
+    assert _check_msg(L.bc_fhe_modulus_switch_check, 8, 4, 12289, 12289) == (
+        E, "New modulus (12289) must be < old modulus (12289)")
+    assert _check_msg(L.bc_fhe_modulus_switch_check, 10, 4, 12289, 6145) == (
+        E, "Input must have 8 elements (degree=4, u64 emulated), got 10")
+    assert _check_msg(L.bc_fhe_key_switch_check, 8, 4, 17, 1, 3) == (
+        E, "Decomposition base must be in [2, 2^24], got 1")
+    assert _check_msg(L.bc_fhe_key_switch_check, 8, 4, 17, (1 << 24) + 1, 3) == (
+        E, "Decomposition base must be in [2, 2^24], got 16777217")
+    assert _check_msg(L.bc_fhe_key_switch_check, 8, 4, 17, 16, 33) == (
+        E, "Decomposition levels must be in [1, 32], got 33")
+    assert _check_msg(L.bc_fhe_key_switch_check, 4, 4, 17, 16, 3) == (
+        E, "Input must have 8 elements (degree=4, u64 emulated), got 4")
+    assert L.bc_fhe_rotate_check(8, 4, -2, 17) == 0
+    assert L.bc_fhe_modulus_switch_check(8, 4, 1, 0) == 0   # q_new = 0 < q_old = 1 passes
+    assert L.bc_fhe_key_switch_check(8, 4, 0, 1 << 24, 32) == 0
+
+
+def test_op_rejection_fixtures(kats):
+    """Every constructor rejection the ops' own unit tests assert."""
+    L = N.lib()
+    fns = {"rotate": L.bc_fhe_rotate_check, "modulus_switch": L.bc_fhe_modulus_switch_check,
+           "key_switch": L.bc_fhe_key_switch_check}
+    for op, args, expect_err in kats["op_rejections"]["values"]:
+        assert (fns[op](*args) != 0) == expect_err, (op, args)
+
+
+def test_rotation_galois_matches_oracle():
+    L = N.lib()
+    for d in (4, 8, 1024, 1 << 16):
+        for r in sorted({-d // 2, -3 % (d // 2 + 1), -1, 0, 1, 2, d // 2}):
+            assert L.bc_rotation_galois(d, r) == O.lib().orc_ref_rotate_galois(d, r)
+        assert L.bc_rotation_galois(d, d // 2 + 1) == 0
+
+
 class _Shape:
     """Stands in for a device tensor: only len() is consulted by new()."""
 
@@ -132,6 +182,14 @@ def test_python_mirror_raises_like_rust():
         bc.FhePointwiseMul.new(_Shape(8), _Shape(8), 2, 17)
     with pytest.raises(bc.BarracudaError):
         bc.FheFastPolyMul.new(_Shape(8), _Shape(6), 4, 17, 4)
+    with pytest.raises(bc.BarracudaError) as e:
+        bc.FheRotate.new(_Shape(8), 4, 3, 12289)
+    assert e.value.kind == "InvalidInput"
+    assert str(e.value) == "Invalid input: Rotation 3 out of range [-2, 2] for degree 4"
+    with pytest.raises(bc.BarracudaError):
+        bc.FheModulusSwitch.new(_Shape(8), 4, 12289, 12289)
+    with pytest.raises(bc.BarracudaError):
+        bc.FheKeySwitch.new(_Shape(8), 4, 12289, 1 << 16, 0)
 
 
 def test_roots_match_reference_restatement():

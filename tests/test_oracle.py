@@ -83,6 +83,20 @@ def test_golden_cases(kats):
             a, b, cc = c["a"], c["b"], c["c"]
             lhs = O.ref_poly_add(O.ref_poly_add(a, b, q), cc, q)
             assert (lhs == O.ref_poly_add(a, O.ref_poly_add(b, cc, q), q)).all()
+        elif k == "rotate":
+            n, q, x = c["degree"], c["modulus"], c["input"]
+            for r in c["rotations"]:
+                x = O.ref_rotate(x, n, r, q)
+            assert [int(v) for v in x] == c["expect"], c["name"]
+            for r in c.get("same_as_rotations", []):
+                assert (O.ref_rotate(c["input"], n, r, q) == x).all(), c["name"]
+        elif k == "modulus_switch":
+            x, qo, qn = c["input"], c["modulus_old"], c["modulus_new"]
+            assert [int(v) for v in O.ref_modulus_switch(x, qo, qn)] == c["expect"], c["name"]
+            assert [int(v) for v in O.exact_modulus_switch(x, qo, qn)] == c["exact"], c["name"]
+        elif k == "key_switch":
+            got = O.ref_key_switch(c["input"], c["decomp_base"], c["decomp_levels"])
+            assert [int(v) for v in got] == c["expect"], c["name"]
         else:
             raise AssertionError(f"unknown kind {k}")
 
@@ -222,3 +236,63 @@ def test_poly_ops_restatement_vs_exact():
     q = 2147352577
     a = np.array([q - 1, q - 2, 123456789], np.uint64)
     assert (O.ref_poly_mul(a, a, q) != O.exact_poly_mul(a, a, q)).all()
+
+
+def _py_automorphism(x, n, g, q):
+    out = [0] * n
+    for i, v in enumerate(int(t) for t in x):
+        p = i * g % (2 * n)
+        out[p % n] = ((q - v) % 2**64 if v else 0) if p >= n else v
+    return out
+
+
+@pytest.mark.parametrize("n", [4, 8, 64, 1024])
+def test_rotate_oracle_is_the_ring_automorphism(n):
+    """FheRotate's map is X -> X^g on Z_q[X]/(X^N + 1): it agrees with a
+    Python restatement, composes by multiplying galois elements mod 2N, and
+    is a ring homomorphism of the negacyclic product (inputs below q)."""
+    rng = np.random.default_rng(n)
+    q = O.ntt_prime(30, n, 0)
+    a, b = random_poly(rng, n, q), random_poly(rng, n, q)
+    for r in sorted({-n // 2, -1, 0, 1, 3 % (n // 2 + 1), n // 2}):
+        g = L.orc_ref_rotate_galois(n, r)
+        ra = O.ref_rotate(a, n, r, q)
+        assert [int(v) for v in ra] == _py_automorphism(a, n, g, q)
+        assert (ra == O.automorphism(a, n, g, q)).all()
+        prod = O.negacyclic_convolution(a, b, n, q)
+        assert (O.ref_rotate(prod, n, r, q) ==
+                O.negacyclic_convolution(ra, O.ref_rotate(b, n, r, q), n, q)).all()
+        for g2 in (3, 2 * n - 1):
+            both = O.automorphism(ra, n, g2, q)
+            assert (both == O.automorphism(a, n, g * g2 % (2 * n), q)).all()
+    assert (O.ref_rotate(a, n, 0, q) == a).all()
+
+
+def test_modulus_switch_restatement_vs_exact():
+    """The shader's wrapping u64 product equals the exact rounding wherever
+    c * q_new < 2^64 (and q_old <= 2^63); the exact map agrees with Python
+    integers everywhere."""
+    rng = np.random.default_rng(5)
+    for _ in range(3000):
+        qo = int(rng.integers(2, 2**int(rng.integers(2, 65)), dtype=np.uint64, endpoint=False)) | 1
+        qn = int(rng.integers(0, qo, dtype=np.uint64))
+        c = int(rng.integers(0, 2**64, dtype=np.uint64))
+        want = ((2 * c * qn + qo) // (2 * qo)) % qn if qn else 0
+        assert L.orc_exact_modulus_switch1(c, qo, qn) == want, (c, qo, qn)
+        if c * qn < 2**64 and qo <= 2**63:
+            assert L.orc_ref_modulus_switch1(c, qo, qn) == want, (c, qo, qn)
+    assert L.orc_ref_modulus_switch1(5, 1, 0) == 0 and L.orc_exact_modulus_switch1(5, 1, 0) == 0
+
+
+def test_decompose_oracle_digits():
+    rng = np.random.default_rng(3)
+    x = rng.integers(0, 2**64, 257, dtype=np.uint64)
+    for base, levels in ((2, 64 // 2), (16, 16), (1 << 16, 4), (1 << 24, 3), (12289, 5), (3, 32)):
+        levels = min(levels, 32)
+        d = O.decompose(x, base, levels)
+        for i in (0, 1, 100, 256):
+            v = int(x[i])
+            for l in range(levels):
+                assert int(d[l, i]) == (v // base**l) % base
+    # FheKeySwitch's net effect is a copy of its input
+    assert (O.ref_key_switch(x, 1 << 16, 3) == x).all()
