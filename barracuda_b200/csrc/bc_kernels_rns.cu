@@ -33,6 +33,15 @@ __device__ __forceinline__ void st_cluster_u64(uint32_t addr, uint64_t v) {
     asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
 }
 
+// Cluster barrier without memory ordering, for the barrier that only keeps
+// a CTA from overwriting a peer's shared memory before the peer has read
+// it: every value read before it has already been consumed by a store
+// instruction, so the reads are complete, and a release would make the
+// barrier wait for the HBM stores as well.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
 // fhe_rotate.wgsl:52-63: 0 stays 0, otherwise q - x with 64-bit wrap-around.
 __device__ __forceinline__ uint64_t negate_mod(uint64_t x, uint64_t q) { return x == 0 ? 0 : q - x; }
 
@@ -42,20 +51,35 @@ __device__ __forceinline__ uint64_t negate_mod(uint64_t x, uint64_t q) { return 
 // negation of input t - N otherwise (g^-1 is odd, so N g^-1 = N mod 2N and
 // the two candidates differ by exactly N).  Writes are coalesced; reads are
 // a permutation of one polynomial, served from L2.
+// Each thread keeps kGatherILP gathers in flight (the kernel is bound by
+// L2 latency, not bandwidth).  Index arithmetic is 32-bit: 2N divides 2^32.
+constexpr uint32_t kGatherILP = 4;
+
 __global__ void k_automorph_gather(KArgs a, uint32_t ginv, const CoeffConst *consts, uint64_t single_q) {
     const uint32_t L = a.logn;
-    const uint64_t N = 1ull << L, mask2 = 2 * N - 1;
+    const uint32_t N = 1u << L, mask2 = 2 * N - 1;
+    const uint32_t S = gridDim.x * blockDim.x;
     const uint64_t polys = static_cast<uint64_t>(a.batch) * a.n_limbs;
     for (uint64_t pl = blockIdx.y; pl < polys; pl += gridDim.y) {
         const uint64_t limb = pl / a.batch, poly = pl % a.batch;
         const uint64_t q = consts ? consts[limb].q : single_q;
         const int64_t base = static_cast<int64_t>(limb) * a.limb_stride + static_cast<int64_t>(poly) * a.poly_stride;
         const uint64_t *in = a.in + base;
-        for (uint64_t j = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; j < N;
-             j += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-            const uint64_t t = (j * ginv) & mask2;
-            const uint64_t x = __ldg(in + (t & (N - 1)));
-            __stcs(a.out + base + j, (t >> L) ? negate_mod(x, q) : x);
+        uint64_t *out = a.out + base;
+        for (uint32_t j0 = blockIdx.x * blockDim.x + threadIdx.x; j0 < N; j0 += kGatherILP * S) {
+            uint64_t x[kGatherILP];
+            uint32_t t[kGatherILP];
+#pragma unroll
+            for (uint32_t k = 0; k < kGatherILP; ++k) {
+                const uint32_t j = j0 + k * S;
+                t[k] = (j * ginv) & mask2;
+                x[k] = j < N ? __ldcg(in + (t[k] & (N - 1))) : 0;  // L2 only: L1 sees no reuse
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < kGatherILP; ++k) {
+                const uint32_t j = j0 + k * S;
+                if (j < N) __stcs(out + j, (t[k] >> L) ? negate_mod(x[k], q) : x[k]);
+            }
         }
     }
 }
@@ -180,7 +204,7 @@ __global__ void __launch_bounds__(kClusterThreads, 2)
                 const uint64_t x = buf[u & (B - 1)];
                 __stcs(dst + static_cast<size_t>(jh) * C, (u & B) ? negate_mod(x, q) : x);
             }
-            cl.sync();
+            cluster_sync_relaxed();
             continue;
         }
         // 2. permute within the class (into registers) ...
@@ -207,7 +231,7 @@ __global__ void __launch_bounds__(kClusterThreads, 2)
             const uint32_t p = k * T + threadIdx.x;
             __stcs(dst + p, buf[(p & (C - 1)) * kStride + (p >> LOGC)]);
         }
-        cl.sync();
+        cluster_sync_relaxed();
     }
 }
 
@@ -262,33 +286,37 @@ int launch_automorph_cluster(const KArgs &a, uint32_t galois, uint32_t ginv, con
 //   constant Pp = floor(P 2^64 / Q) (at most one below), the remainder
 //   b P - t Q (< 2Q, held in 65 bits) corrects it and decides the rounding.
 //   t + round <= P, so the final reduction is one comparison.
+__device__ __forceinline__ uint64_t modulus_switch_one(uint64_t x, const ModSwitchConst &c) {
+    if (c.q_new == 0) return 0;
+    uint64_t b = x;
+    if (b >= c.q_old) {  // inputs are usually already below q_old
+        b = x - __umul64hi(x, c.m_old) * c.q_old;
+        if (b >= c.q_old) b -= c.q_old;
+    }
+    uint64_t t = __umul64hi(b, c.p_shoup);
+    const uint64_t lo1 = b * c.q_new, lo2 = t * c.q_old;
+    uint64_t rem = lo1 - lo2;
+    // the remainder is below 2 q_old: 64 bits hold it unless q_old > 2^63
+    const bool over = c.q_old > (1ull << 63)
+                          ? (__umul64hi(b, c.q_new) - __umul64hi(t, c.q_old) - (lo1 < lo2 ? 1 : 0)) != 0
+                          : false;
+    if (over || rem >= c.q_old) {
+        rem -= c.q_old;
+        ++t;
+    }
+    if (rem >= c.q_old - rem) ++t;
+    return t == c.q_new ? 0 : t;
+}
+
+// Two words per thread per iteration, both loads issued first.
 __global__ void k_modulus_switch(const uint64_t *__restrict__ in, uint64_t *__restrict__ out, size_t count,
                                  ModSwitchConst c) {
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const uint64_t x = __ldcs(in + i);
-        uint64_t r = 0;
-        if (c.q_new != 0) {
-            uint64_t b = x;
-            if (b >= c.q_old) {  // inputs are usually already below q_old
-                b = x - __umul64hi(x, c.m_old) * c.q_old;
-                if (b >= c.q_old) b -= c.q_old;
-            }
-            uint64_t t = __umul64hi(b, c.p_shoup);
-            const uint64_t lo1 = b * c.q_new, lo2 = t * c.q_old;
-            uint64_t rem = lo1 - lo2;
-            // the remainder is below 2 q_old: 64 bits hold it unless q_old > 2^63
-            const bool over = c.q_old > (1ull << 63)
-                                  ? (__umul64hi(b, c.q_new) - __umul64hi(t, c.q_old) - (lo1 < lo2 ? 1 : 0)) != 0
-                                  : false;
-            if (over || rem >= c.q_old) {
-                rem -= c.q_old;
-                ++t;
-            }
-            if (rem >= c.q_old - rem) ++t;
-            r = t == c.q_new ? 0 : t;
-        }
-        __stcs(out + i, r);
+    const size_t S = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count; i += 2 * S) {
+        const bool second = i + S < count;
+        const uint64_t x0 = __ldcs(in + i), x1 = second ? __ldcs(in + i + S) : 0;
+        __stcs(out + i, modulus_switch_one(x0, c));
+        if (second) __stcs(out + i + S, modulus_switch_one(x1, c));
     }
 }
 
@@ -374,10 +402,10 @@ int launch_automorphism(const KArgs &a, uint32_t galois, const CoeffConst *const
     // Kernel for N above the shared-memory size.  Measured on B200 (16-limb
     // batches of 2^28 words, fraction of HBM copy bandwidth):
     //   N        gather  scatter  cluster  cluster+direct
-    //   2^14      0.33    0.46     0.50     0.63
-    //   2^15      0.45    0.46     0.40     0.37
-    //   2^16      0.47    0.40     0.32     0.33
-    //   2^17      0.50    0.26     0.24     0.19
+    //   2^14      0.45    0.46     0.50     0.67
+    //   2^15      0.55    0.46     0.41     0.39
+    //   2^16      0.55    0.40     0.33     0.35
+    //   2^17      0.54    0.27     0.25     0.20
     // BARRACUDA_AUTOMORPH_KERNEL=gather|scatter|cluster|direct overrides.
     static const int forced = [] {
         const char *e = std::getenv("BARRACUDA_AUTOMORPH_KERNEL");

@@ -521,6 +521,78 @@ def run_sweep(args):
     dev.close()
 
 
+# --kernel-case: one kernel family alone on a small case (256 MiB per
+# operand, larger than L2), for ncu captures of the kernels around the
+# transform.  name -> (log2 N, limbs, kernel name, algorithmic bytes per word)
+KERNEL_CASES = {
+    "polymul": (15, 32, "k_polymul_fast", 40),       # NTT(B) into C, then the fused kernel
+    "automorphism_smem": (13, 16, "k_automorph_smem", 16),
+    "automorphism_cluster": (14, 16, "k_automorph_cluster", 16),
+    "automorphism_gather": (16, 16, "k_automorph_gather", 16),
+    "coeff_add": (16, 16, "k_coeff", 24),
+    "coeff_mul": (16, 16, "k_coeff", 24),
+    "pointwise": (16, 16, "k_pointwise", 24),
+    "modulus_switch": (16, 16, "k_modulus_switch", 16),
+    "decompose": (16, 16, "k_decompose", 32),            # base 2^16, 3 digits
+}
+
+
+def run_kernel_case(args):
+    """Warm-up + timed launches of one kernel family (KERNEL_CASES), one
+    JSON line with the CUDA-event mean and the fraction of HBM peak."""
+    import torch
+
+    import barracuda_b200 as bc
+
+    case = args.kernel_case
+    logn, limbs, kernel, bytes_per_word = KERNEL_CASES[case]
+    torch.cuda.set_device(0)
+    dev = bc.Device(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sh = stream.cuda_stream
+    hbm, peak_kind = peaks()
+    n = 1 << logn
+    words = 1 << 25
+    batch = words // (n * limbs)
+    qs = bc.ntt_primes(31, n, limbs)
+    plan = bc.NttPlan(dev, n, qs, [bc.negacyclic_root(q, n) for q in qs], mode=bc.NEGACYCLIC)
+    a = torch.empty(words, dtype=torch.int64, device="cuda")
+    b = torch.empty_like(a)
+    c = torch.empty(words * (3 if case == "decompose" else 1), dtype=torch.int64, device="cuda")
+    plan.fill_uniform(a, batch, seed=1, stream=sh)
+    plan.fill_uniform(b, batch, seed=2, stream=sh)
+    ops = {
+        "polymul": lambda: plan.polymul(a, b, c, batch, stream=sh),
+        "automorphism_smem": lambda: plan.automorphism(a, c, batch, 2469, stream=sh),
+        "automorphism_cluster": lambda: plan.automorphism(a, c, batch, 2469, stream=sh),
+        "automorphism_gather": lambda: plan.automorphism(a, c, batch, 2469, stream=sh),
+        "coeff_add": lambda: plan.poly_add(a, b, c, batch, stream=sh),
+        "coeff_mul": lambda: plan.poly_mul(a, b, c, batch, stream=sh),
+        "pointwise": lambda: plan.pointwise_mul(a, b, c, batch, stream=sh),
+        "modulus_switch": lambda: bc.modulus_switch(dev, a, c, words, qs[0], qs[1] >> 8, stream=sh),
+        "decompose": lambda: bc.decompose(dev, a, c, words, 1 << 16, 3, stream=sh),
+    }
+    fn = ops[case]
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    gbs = words * bytes_per_word / (ms / 1000.0) / 1e9
+    print(json.dumps({"kernel_case": case, "kernel": kernel, "N": n, "limbs": limbs, "batch": batch,
+                      "words": words, "bytes_per_word": bytes_per_word, "ms": ms, "gb_per_s": gbs,
+                      "frac": gbs / hbm, "peak_gbs": hbm, "peak_kind": peak_kind,
+                      "launches_before_timed": args.warmup}), flush=True)
+    plan.close()
+    dev.close()
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -537,10 +609,14 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="per-N forward/inverse report (config 4 shape) instead of the bench line")
+    ap.add_argument("--kernel-case", choices=sorted(KERNEL_CASES),
+                    help="time one kernel family on a small case (for ncu captures)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
-    if args.sweep:
+    if args.kernel_case:
+        run_kernel_case(args)
+    elif args.sweep:
         run_sweep(args)
     elif args.impl == "reference":
         run_reference(args)
