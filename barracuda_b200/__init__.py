@@ -14,6 +14,6 @@ from .ops import (  # noqa: F401
 )
 from .plan import (  # noqa: F401
     NttPlan, Layout, CYCLIC, NEGACYCLIC, ntt_prime, ntt_primes, negacyclic_root, partition, digest,
-    modulus_switch, decompose,
+    modulus_switch, decompose, calibrate_butterflies,
 )
 from .shard import Shard, ShardGroup, ShardFailure, job_digest  # noqa: F401

@@ -132,6 +132,7 @@ SIGNATURES = {
     "bc_decompose": (_i32, [_vp, _vp, _vp, _sz, _u32, _u32, _vp]),
     "bc_fill_uniform": (_i32, [_vp, _vp, _u32, _lay, _u64, _u64, _u64, _vp]),
     "bc_digest": (_i32, [_vp, _vp, _sz, _u64, _vp, _vp]),
+    "bc_calibrate_butterflies": (_i32, [_vp, _i32, ctypes.POINTER(ctypes.c_double)]),
     "bc_partition": (_i32, [_u64, _u32, _u32, _u64p, _u64p]),
     "bc_ntt_prime": (_u64, [_u32, _u32, _u32]),
     "bc_negacyclic_root": (_u64, [_u64, _u32]),

@@ -224,9 +224,9 @@ int run_ntt(bc_ctx *ctx, const uint64_t *in, uint32_t degree, uint64_t modulus, 
             uint64_t *out) {
     int st = check_width(modulus);
     if (st) return st;
-    bc_plan *p = nullptr;
-    if ((st = bc::cached_plan(ctx, degree, modulus, root, 0, BC_NTT_CYCLIC, &p))) return st;
-    if ((st = bc::run_forward(p, in, out, 1, nullptr, ctx->stream))) return st;
+    std::shared_ptr<bc_plan> sp;
+    if ((st = bc::cached_plan(ctx, degree, modulus, root, 0, BC_NTT_CYCLIC, &sp))) return st;
+    if ((st = bc::run_forward(sp.get(), in, out, 1, nullptr, ctx->stream))) return st;
     return bc::ctx_sync(ctx);
 }
 
@@ -234,10 +234,10 @@ int run_intt(bc_ctx *ctx, const uint64_t *in, uint32_t degree, uint64_t modulus,
              uint64_t *out) {
     int st = check_width(modulus);
     if (st) return st;
-    bc_plan *p = nullptr;
+    std::shared_ptr<bc_plan> sp;
     // cyclic plan whose inverse table is built from inv_root
-    if ((st = bc::cached_plan(ctx, degree, modulus, 0, inv_root, BC_NTT_CYCLIC, &p))) return st;
-    if ((st = bc::run_inverse(p, in, out, 1, nullptr, ctx->stream))) return st;
+    if ((st = bc::cached_plan(ctx, degree, modulus, 0, inv_root, BC_NTT_CYCLIC, &sp))) return st;
+    if ((st = bc::run_inverse(sp.get(), in, out, 1, nullptr, ctx->stream))) return st;
     return bc::ctx_sync(ctx);
 }
 
@@ -262,9 +262,9 @@ int run_pointwise(bc_ctx *ctx, const uint64_t *a, const uint64_t *b, uint32_t de
         return bc::ctx_sync(ctx);
     }
     if ((st = check_width(modulus))) return st;
-    bc_plan *p = nullptr;
-    if ((st = bc::cached_plan(ctx, degree, modulus, 0, 0, BC_NTT_CYCLIC, &p))) return st;
-    if ((st = bc::run_pointwise(p, a, b, out, 1, nullptr, ctx->stream))) return st;
+    std::shared_ptr<bc_plan> sp;
+    if ((st = bc::cached_plan(ctx, degree, modulus, 0, 0, BC_NTT_CYCLIC, &sp))) return st;
+    if ((st = bc::run_pointwise(sp.get(), a, b, out, 1, nullptr, ctx->stream))) return st;
     return bc::ctx_sync(ctx);
 }
 
@@ -276,9 +276,9 @@ int run_fast_poly_mul(bc_ctx *ctx, const uint64_t *a, const uint64_t *b, uint32_
     if (st) return st;
     if ((st = check_width(modulus))) return st;
     const uint64_t inv_root = bc::ref_fastmul_modinv(root, modulus);
-    bc_plan *p = nullptr;
-    if ((st = bc::cached_plan(ctx, degree, modulus, root, inv_root, BC_NTT_CYCLIC, &p))) return st;
-    if ((st = bc::run_polymul(p, a, b, out, 1, nullptr, ctx->stream))) return st;
+    std::shared_ptr<bc_plan> sp;
+    if ((st = bc::cached_plan(ctx, degree, modulus, root, inv_root, BC_NTT_CYCLIC, &sp))) return st;
+    if ((st = bc::run_polymul(sp.get(), a, b, out, 1, nullptr, ctx->stream))) return st;
     return bc::ctx_sync(ctx);
 }
 

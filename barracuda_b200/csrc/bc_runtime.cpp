@@ -264,22 +264,21 @@ int make_args(bc_plan *p, const uint64_t *in, const uint64_t *in2, uint64_t *out
     return BC_OK;
 }
 
-int ensure_scratch(bc_plan *p, size_t bytes, cudaStream_t s) {
-    std::lock_guard<std::mutex> lk(p->scratch_mu);
-    if (p->scratch_bytes >= bytes) return BC_OK;
-    if (p->d_scratch) {
-        cudaStreamSynchronize(s);
-        cudaFree(p->d_scratch);
-        p->d_scratch = nullptr;
-        p->scratch_bytes = 0;
-    }
-    const cudaError_t e = cudaMalloc(&p->d_scratch, bytes);
-    if (e != cudaSuccess) return cuda_fail(e, "scratch allocation");
-    p->scratch_bytes = bytes;
-    return BC_OK;
-}
-
 size_t wbytes(Word w) { return w == Word::W64 ? 8 : 4; }
+
+// Multi-pass transform with a temporary from the context's stream-ordered
+// pool: allocated and freed on `s` around the launches, so it is private to
+// this call and outlives its kernels without any synchronization.
+int run_global(bc_plan *p, bool gs, bool inverse, const KArgs &a, uint32_t batch, cudaStream_t s) {
+    const size_t need = wbytes(p->word) * (static_cast<size_t>(batch) * p->n_limbs) << p->logn;
+    void *scratch = nullptr;
+    cudaError_t e = cudaMallocFromPoolAsync(&scratch, need, p->ctx->pool, s);
+    if (e != cudaSuccess) return cuda_fail(e, "transform scratch");
+    const int st = launch_ntt_global(p->word, gs, inverse, a, scratch, s);
+    e = cudaFreeAsync(scratch, s);
+    if (st) return st;
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "transform scratch release");
+}
 
 // The fast kernels move pairs of coefficients as 16-byte words.
 bool fast_layout_ok(const KArgs &a) {
@@ -306,17 +305,9 @@ int run_transform(bc_plan *p, bool inverse, const uint64_t *in, uint64_t *out, u
         }
         if (p->logn <= smem_max_logn(p->word)) return launch_ntt_smem(p->word, gs, inverse, a, s);
         [[fallthrough]];
-    case KernelKind::Global: {
-        const size_t need = wbytes(p->word) * (static_cast<size_t>(batch) * p->n_limbs) << p->logn;
-        if ((st = ensure_scratch(p, need, s))) return st;
-        return launch_ntt_global(p->word, gs, inverse, a, p->d_scratch, s);
-    }
+    case KernelKind::Global: return run_global(p, gs, inverse, a, batch, s);
     case KernelKind::Smem: return launch_ntt_smem(p->word, gs, inverse, a, s);
-    default: {
-        const size_t need = wbytes(p->word) * (static_cast<size_t>(batch) * p->n_limbs) << p->logn;
-        if ((st = ensure_scratch(p, need, s))) return st;
-        return launch_ntt_global(p->word, gs, inverse, a, p->d_scratch, s);
-    }
+    default: return run_global(p, gs, inverse, a, batch, s);
     }
 }
 
@@ -429,7 +420,7 @@ int run_polymul(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t *c, 
 }
 
 int cached_plan(bc_ctx *ctx, uint32_t degree, uint64_t modulus, uint64_t root, uint64_t inv_root,
-                int mode, bc_plan **out) {
+                int mode, std::shared_ptr<bc_plan> *out) {
     std::lock_guard<std::mutex> lk(ctx->cache_mu);
     for (auto it = ctx->cache.begin(); it != ctx->cache.end(); ++it) {
         if (it->degree == degree && it->modulus == modulus && it->root == root &&
@@ -443,12 +434,11 @@ int cached_plan(bc_ctx *ctx, uint32_t degree, uint64_t modulus, uint64_t root, u
     const int st = bc_plan_create(ctx, degree, 1, &modulus, &root,
                                   mode == BC_NTT_CYCLIC ? &inv_root : nullptr, mode, &p);
     if (st) return st;
-    ctx->cache.push_front({degree, modulus, root, inv_root, mode, p});
-    while (ctx->cache.size() > 32) {
-        bc_plan_destroy(ctx->cache.back().plan);
-        ctx->cache.pop_back();
-    }
-    *out = p;
+    std::shared_ptr<bc_plan> sp(p, [](bc_plan *q) { bc_plan_destroy(q); });
+    ctx->cache.push_front({degree, modulus, root, inv_root, mode, sp});
+    // an evicted plan still in use by another caller goes when that caller ends
+    while (ctx->cache.size() > 32) ctx->cache.pop_back();
+    *out = std::move(sp);
     return BC_OK;
 }
 
@@ -504,6 +494,20 @@ int bc_ctx_create(int device, bc_ctx **out) {
         delete c;
         return cuda_fail(e, "status word allocation");
     }
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    if ((e = cudaMemPoolCreate(&c->pool, &props)) != cudaSuccess) {
+        cudaFree(c->d_status);
+        cudaStreamDestroy(c->stream);
+        delete c;
+        return cuda_fail(e, "memory pool creation");
+    }
+    // keep freed temporaries in the pool instead of returning them at every
+    // synchronization (the pool belongs to this context only)
+    uint64_t keep = UINT64_MAX;
+    cudaMemPoolSetAttribute(c->pool, cudaMemPoolAttrReleaseThreshold, &keep);
     *out = c;
     return BC_OK;
 }
@@ -512,10 +516,11 @@ int bc_ctx_destroy(bc_ctx *ctx) {
     if (!ctx) return BC_OK;
     use_device(ctx);
     cudaStreamSynchronize(ctx->stream);
-    for (auto &e : ctx->cache) bc_plan_destroy(e.plan);
-    ctx->cache.clear();
+    ctx->cache.clear();  // destroys the cached plans (no caller holds one now)
     cudaFree(ctx->d_status);
     cudaStreamDestroy(ctx->stream);
+    // returns at once; the pool goes once its last stream-ordered free completes
+    if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
     delete ctx;
     return BC_OK;
 }
@@ -680,7 +685,6 @@ int bc_plan_destroy(bc_plan *p) {
     cudaFree(p->d_tw_inv);
     cudaFree(p->d_tw_fwd_fast);
     cudaFree(p->d_tw_inv_fast);
-    cudaFree(p->d_scratch);
     delete p;
     return BC_OK;
 }

@@ -20,12 +20,16 @@ struct bc_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
     uint32_t *d_status = nullptr;
+    // Stream-ordered pool for per-call temporaries (multi-pass transforms):
+    // each call allocates and frees on its own stream, so calls on several
+    // streams never share or free a buffer another stream still uses.
+    cudaMemPool_t pool = nullptr;
     std::mutex cache_mu;
     struct CacheEntry {
         uint32_t degree;
         uint64_t modulus, root, inv_root;
         int mode;
-        bc_plan *plan;
+        std::shared_ptr<bc_plan> plan;  // callers hold a reference while they use it
     };
     std::list<CacheEntry> cache;  // most recent first
 };
@@ -48,9 +52,6 @@ struct bc_plan {
     void *d_tw_fwd_fast = nullptr;  // the same tables in the fast kernels' layout
     void *d_tw_inv_fast = nullptr;
     uint64_t table_bytes = 0;
-    std::mutex scratch_mu;
-    void *d_scratch = nullptr;
-    size_t scratch_bytes = 0;
 };
 
 namespace bc {
@@ -66,9 +67,11 @@ void table_entry(const bc_plan &p, uint32_t limb, int table, uint32_t k, uint64_
 int plan_build_host(bc_plan &p, uint32_t degree, uint32_t n_limbs, const uint64_t *moduli,
                     const uint64_t *roots, const uint64_t *inv_roots, int mode,
                     std::vector<unsigned char> *fwd, std::vector<unsigned char> *inv);
-// Plan for the reference-op entry points, cached per context.
+// Plan for the reference-op entry points, cached per context.  The caller's
+// reference keeps the plan alive if the cache evicts it meanwhile (another
+// thread filling the cache), so it is destroyed only after its last use.
 int cached_plan(bc_ctx *ctx, uint32_t degree, uint64_t modulus, uint64_t root,
-                uint64_t inv_root, int mode, bc_plan **out);
+                uint64_t inv_root, int mode, std::shared_ptr<bc_plan> *out);
 // Waits for the context stream and converts kernel status bits to errors.
 int ctx_sync(bc_ctx *ctx);
 

@@ -160,5 +160,12 @@ def decompose(device: Device, src, dst, count: int, base: int, levels: int, stre
                              stream or None))
 
 
+def calibrate_butterflies(device: Device, word_bits: int = 32) -> float:
+    """Register-only modular butterflies per second on this GPU (roofline's integer term)."""
+    out = ctypes.c_double()
+    check(lib().bc_calibrate_butterflies(device.handle, word_bits, ctypes.byref(out)))
+    return out.value
+
+
 def digest(device: Device, buf, count: int, out, stream: int = 0, first_index: int = 0):
     check(lib().bc_digest(device.handle, _ptr(buf), count, first_index, _ptr(out), stream or None))

@@ -327,6 +327,18 @@ def _run_ours(args, torch, bc, group, world, rank, local):
                 "avg_launch_ms": fwd_avg, "inverse_avg_launch_ms": inv_avg,
                 "traffic": (NCU_TRAFFIC_PER_TRANSFORM * polys * LIMBS
                             if NCU_TRAFFIC_PER_TRANSFORM else None)}
+    # The roofline's second term: (N/2) log2 N butterflies per transform at
+    # the integer-pipe peak, measured live on this GPU with the plans' own
+    # 32-bit arithmetic (after the timed region).
+    bfly = bc.calibrate_butterflies(dev, 32)
+    int_rate = bfly / ((N // 2) * N_LOG)
+    hbm_rate = hbm * 1e9 / BYTES_PER_TRANSFORM
+    launch_rate = polys * LIMBS / (fwd_avg / 1000.0)
+    roofline["integer_peak"] = {"butterflies_per_s": bfly, "limb_transforms_per_s": int_rate,
+                                "word_bits": 32, "measured": "bc_calibrate_butterflies, register-only"}
+    roofline["hbm_limb_transforms_per_s"] = hbm_rate
+    roofline["binding_term"] = "hbm" if hbm_rate <= int_rate else "integer"
+    roofline["frac_of_binding_term"] = launch_rate / min(hbm_rate, int_rate)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -234,7 +234,11 @@ int bc_plan_info_get(const bc_plan *plan, bc_plan_info *out);
 
 /* Forward / inverse transform of `batch` polynomials per limb (all limbs).
  * In place (d_in == d_out) is allowed.  Asynchronous on `stream`
- * (NULL: the context stream). */
+ * (NULL: the context stream).  The multi-pass path (kernel_kind 2, and
+ * layouts the fast kernels cannot take above the shared-memory size) takes
+ * a batch-sized temporary from the context's stream-ordered memory pool and
+ * returns it on the same stream: calls on one plan from several streams or
+ * threads never share it, and no call synchronizes. */
 int bc_ntt_forward(bc_plan *plan, const uint64_t *d_in, uint64_t *d_out, uint32_t batch,
                    const bc_layout *layout, void *stream);
 int bc_ntt_inverse(bc_plan *plan, const uint64_t *d_in, uint64_t *d_out, uint32_t batch,
@@ -332,6 +336,14 @@ int bc_fill_uniform(bc_plan *plan, uint64_t *d_out, uint32_t batch, const bc_lay
  * whole array, whatever the number of GPUs. */
 int bc_digest(bc_ctx *ctx, const uint64_t *d_in, size_t count, uint64_t first_index,
               uint64_t *d_out, void *stream);
+
+/* Integer-pipe peak of this GPU for the plans' butterfly arithmetic
+ * (word_bits 32: q < 2^31 Shoup with lazy [0, 2q) reduction; 64: q < 2^62
+ * Shoup/Harvey): register-only Cooley-Tukey butterflies on every SM, timed
+ * with CUDA events on the context stream.  The NTT roofline is the slower
+ * of 16N bytes at HBM bandwidth and (N/2) log2 N butterflies at this rate.
+ * Takes a few milliseconds; synchronizes the context stream. */
+int bc_calibrate_butterflies(bc_ctx *ctx, int word_bits, double *butterflies_per_s);
 
 /* ------------------------------------------------------- multi-GPU split */
 /* Contiguous balanced split of `units` over `shards`: shard s gets

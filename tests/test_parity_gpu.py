@@ -286,6 +286,86 @@ def test_plan_strided_ciphertext_layout_and_in_place(device):
     assert (buf.to_u64() == x).all()
 
 
+def _exact_negacyclic(x, n, q, psi):
+    """Exact O(N log N) negacyclic forward transform of one polynomial (oracle)."""
+    _, out = O.baseline_run("exact_negacyclic_ntt", x, n, [q], [psi], 1)
+    return out
+
+
+@pytest.mark.parametrize("logn,bits", [(18, 31), (18, 60), (19, 31)])
+def test_plan_multipass_global_path(device, logn, bits):
+    """N above the cluster kernels: one launch per stage through a per-call
+    temporary; exact forward values and the round trip."""
+    n, limbs, batch = 1 << logn, 2, 2
+    plan, qs, psis = _plan(device, n, limbs, bits, bc.NEGACYCLIC)
+    assert plan.info["kernel_kind"] == 2
+    total = limbs * batch * n
+    src, dst, back = _alloc(device, total), _alloc(device, total), _alloc(device, total)
+    plan.fill_uniform(src, batch, seed=logn)
+    plan.forward(src, dst, batch)
+    plan.inverse(dst, back, batch)
+    device.synchronize()
+    x, X = src.to_u64(), dst.to_u64()
+    assert (back.to_u64() == x).all()
+    for l, p in ((0, 0), (1, batch - 1)):
+        off = (l * batch + p) * n
+        assert (X[off:off + n] == _exact_negacyclic(x[off:off + n], n, qs[l], psis[l])).all(), (l, p)
+    plan.close()
+
+
+def test_reference_ops_from_threads_evict_cached_plans(device):
+    """bc_fhe_ntt from four threads over 48 (N, q) pairs, more than the
+    context's 32 cached plans: plans evicted while another thread runs on
+    them stay alive until that call ends, and every result is exact."""
+    import threading
+    params = [(1 << (6 + i % 4), O.ntt_prime(30, 1 << (6 + i % 4), i)) for i in range(48)]
+    errors = []
+
+    def worker(tid):
+        rng = np.random.default_rng(tid)
+        try:
+            for k in range(3 * len(params)):
+                n, q = params[(k * 7 + tid * 13) % len(params)]
+                w = pow(O.psi(q, n), 2, q)
+                x = random_poly(rng, n, q)
+                got = ntt(device, x, n, q, w)
+                if not (got == O.ref_ntt(x, n, q, w)).all():
+                    errors.append((tid, n, q))
+        except Exception as e:  # pragma: no cover - reported below
+            errors.append((tid, repr(e)))
+
+    threads = [threading.Thread(target=worker, args=(t,)) for t in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=300)
+    assert not errors, errors[:5]
+
+
+def test_plan_shared_by_two_streams_multipass(device):
+    """One plan, two streams, different batch sizes in flight at once on the
+    multi-pass path: each call has its own temporary, so both results equal
+    the single-stream ones."""
+    import torch
+    n, limbs = 1 << 18, 1
+    plan, qs, psis = _plan(device, n, limbs, 31, bc.NEGACYCLIC)
+    bufs = {}
+    for batch in (2, 6):
+        src, dst = _alloc(device, batch * n), _alloc(device, batch * n)
+        plan.fill_uniform(src, batch, seed=batch)
+        plan.forward(src, dst, batch)
+        device.synchronize()
+        bufs[batch] = (src, dst, dst.to_u64().copy())
+    streams = {2: torch.cuda.Stream(), 6: torch.cuda.Stream()}
+    for _ in range(3):
+        for batch, (src, dst, _) in bufs.items():
+            plan.forward(src, dst, batch, stream=streams[batch].cuda_stream)
+    torch.cuda.synchronize()
+    for batch, (_, dst, want) in bufs.items():
+        assert (dst.to_u64() == want).all(), batch
+    plan.close()
+
+
 @pytest.mark.parametrize("logn,bits", [(12, 31), (14, 31), (15, 31), (16, 31), (17, 31), (13, 60), (15, 60)])
 @pytest.mark.parametrize("mode", [bc.NEGACYCLIC, bc.CYCLIC])
 def test_plan_polymul_matches_chain(device, logn, bits, mode):
