@@ -423,49 +423,71 @@ def run_e2e(args, torch, plan, lay, polys, x, X, group):
 
 
 def run_sweep(args):
-    """Config 4 shape on one GPU: for each N, forward and inverse of a
-    [limb][poly][N] batch of about 2 GiB (u64), one JSON line per N with the
-    launch times and the fraction of the measured HBM peak (16N bytes per
-    limb-transform).  Not the headline bench line; --sweep selects it."""
+    """Config 4: for each N, forward and inverse of a [limb][poly][N] batch of
+    about 2 GiB (u64) per GPU, sharded by limb across the ranks (each GPU
+    owns a contiguous range of the limbs, 32 per GPU below N = 2^14, 16
+    above).  One JSON line per N with the launch times (max over ranks) and
+    the whole-job GB/s as a fraction of the measured HBM peak times the GPU
+    count (16N bytes per limb-transform).  On one GPU it then adds lines
+    for the coefficient-wise ops and the rotation / RNS ops.  Not the
+    headline bench line; --sweep selects it."""
     import torch
 
     import barracuda_b200 as bc
 
-    torch.cuda.set_device(0)
-    dev = bc.Device(0)
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    group = bc.ShardGroup("nccl", timeout=300.0, device=torch.device("cuda", local))
+    try:
+        _run_sweep(args, torch, bc, group, world, rank, local)
+    finally:
+        group.close()
+
+
+def _run_sweep(args, torch, bc, group, world, rank, local):
+    dev = bc.Device(local)
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     sh = stream.cuda_stream
     hbm, peak_kind = peaks()
     for L in range(12, 18):
         n = 1 << L
-        limbs = 32 if L < 14 else 16
-        batch = max(1, (1 << 28) // (n * limbs))
-        qs = bc.ntt_primes(31, n, limbs)
+        per_gpu = 32 if L < 14 else 16
+        limbs_total = per_gpu * world
+        begin, limbs = bc.partition(limbs_total, world, rank)
+        batch = max(1, (1 << 28) // (n * per_gpu))
+        qs = bc.ntt_primes(31, n, limbs_total)[begin:begin + limbs]
         plan = bc.NttPlan(dev, n, qs, [bc.negacyclic_root(q, n) for q in qs], mode=bc.NEGACYCLIC)
         lay = bc.Layout(limb_stride=batch * n, poly_stride=n)
         x = torch.empty(limbs * batch * n, dtype=torch.int64, device="cuda")
         y = torch.empty_like(x)
         plan.fill_uniform(x, batch, seed=1, layout=lay, stream=sh)
-        line = {"sweep": "config4 shape, 1 GPU", "N": n, "limbs": limbs, "batch": batch,
+        line = {"sweep": f"config4 shape, {world} GPU(s), sharded by limb", "N": n, "n_gpus": world,
+                "limbs_total": limbs_total, "limbs_per_gpu": per_gpu, "batch": batch,
                 "peak_gbs": hbm, "peak_kind": peak_kind}
         for name, fn in (("forward", plan.forward), ("inverse", plan.inverse)):
             for _ in range(args.warmup):
                 fn(x, y, batch, layout=lay, stream=sh)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
+            group.barrier()
             e0.record(stream)
             for _ in range(args.steps):
                 fn(x, y, batch, layout=lay, stream=sh)
             e1.record(stream)
             torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / args.steps
-            gbs = limbs * batch * 16 * n / (ms / 1000.0) / 1e9
-            line[name] = {"ms": ms, "limb_transforms_per_s": limbs * batch / (ms / 1000.0),
-                          "gb_per_s": gbs, "frac": gbs / hbm}
-        print(json.dumps(line), flush=True)
+            ms = group.max_f64(e0.elapsed_time(e1)) / args.steps
+            units = limbs_total * batch
+            gbs = units * 16 * n / (ms / 1000.0) / 1e9
+            line[name] = {"ms": ms, "limb_transforms_per_s": units / (ms / 1000.0),
+                          "gb_per_s": gbs, "frac": gbs / (hbm * world)}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
         del x, y
         plan.close()
+    if world > 1:
+        dev.close()
+        return
     # coefficient-wise ops (FhePolyAdd / FhePolySub / FhePolyMul semantics), 24 bytes
     # per coefficient (read a, b; write c), both prime families
     for bits in (31, 60):
