@@ -125,6 +125,8 @@ SIGNATURES = {
     "bc_poly_sub": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_poly_mul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_pointwise_mul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
+    "bc_ntt_forward_mul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
+    "bc_ntt_inverse_mul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_polymul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_polymul_static_scratch": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_automorphism": (_i32, [_vp, _vp, _vp, _u32, _lay, _u32, _vp]),

@@ -5,5 +5,6 @@ namespace bc {
 namespace fast {
 template int dispatch_l<Arith32<false>, 4>(uint32_t L, bool gs, bool scale, const KArgs &a, cudaStream_t s);
 template int dispatch_polymul_l<Arith32<false>, 4>(uint32_t L, const KArgs &a, cudaStream_t s);
+template int dispatch_ntt_mul_l<Arith32<false>, 4>(uint32_t L, bool inverse, const KArgs &a, cudaStream_t s);
 }  // namespace fast
 }  // namespace bc

@@ -56,6 +56,10 @@ int launch_ntt_fast(Word w, bool gs, bool scale_last, const KArgs &a, cudaStream
 // which stores each stage's twiddles transposed per pass (pair = 2 for
 // 8-byte entries, 1 for 16-byte entries).
 int fast_variant_for(Word w, uint32_t logn, bool inverse);
+// Negacyclic transform fused with a pointwise product on the fast schedules
+// (a.in = A, a.in2 = B^, a.out = C, a.tw = that direction's fast table):
+// inverse = false: C = NTT(A) * B^; inverse = true: C = INTT(A * B^).
+int launch_ntt_mul_fast(Word w, bool inverse, const KArgs &a, cudaStream_t s);
 // Fused negacyclic polymul on the fast schedules: a.in = A, a.in2 = NTT(B)
 // in natural order (may alias a.out), a.out = C, a.tw / a.tw2 = the fast
 // forward / inverse tables.  Needs the same variant in both directions.

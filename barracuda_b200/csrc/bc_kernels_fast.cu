@@ -14,6 +14,8 @@ template <class A, int LOGE>
 int dispatch_l(uint32_t L, bool gs, bool scale, const KArgs &a, cudaStream_t s);
 template <class A, int LOGE>
 int dispatch_polymul_l(uint32_t L, const KArgs &a, cudaStream_t s);
+template <class A, int LOGE>
+int dispatch_ntt_mul_l(uint32_t L, bool inverse, const KArgs &a, cudaStream_t s);
 }  // namespace fast
 
 namespace {
@@ -86,6 +88,23 @@ int launch_ntt_fast(Word w, bool gs, bool scale_last, const KArgs &a, cudaStream
         if (v == 7) return fast::dispatch_l<Arith32<false>, 7>(a.logn, gs, scale_last, a, s);
         return fast::dispatch_l<Arith32<false>, 5>(a.logn, gs, scale_last, a, s);
     default: return fast::dispatch_l<Arith64, 4>(a.logn, gs, scale_last, a, s);
+    }
+}
+
+int launch_ntt_mul_fast(Word w, bool inverse, const KArgs &a, cudaStream_t s) {
+    const int v = fast_variant(w, a.logn, inverse);
+    switch (w) {
+    case Word::W32Lazy4:
+        if (v == 4) return fast::dispatch_ntt_mul_l<Arith32<true>, 4>(a.logn, inverse, a, s);
+        if (v == 6) return fast::dispatch_ntt_mul_l<Arith32<true>, 6>(a.logn, inverse, a, s);
+        if (v == 7) return fast::dispatch_ntt_mul_l<Arith32<true>, 7>(a.logn, inverse, a, s);
+        return fast::dispatch_ntt_mul_l<Arith32<true>, 5>(a.logn, inverse, a, s);
+    case Word::W32Lazy2:
+        if (v == 4) return fast::dispatch_ntt_mul_l<Arith32<false>, 4>(a.logn, inverse, a, s);
+        if (v == 6) return fast::dispatch_ntt_mul_l<Arith32<false>, 6>(a.logn, inverse, a, s);
+        if (v == 7) return fast::dispatch_ntt_mul_l<Arith32<false>, 7>(a.logn, inverse, a, s);
+        return fast::dispatch_ntt_mul_l<Arith32<false>, 5>(a.logn, inverse, a, s);
+    default: return fast::dispatch_ntt_mul_l<Arith64, 4>(a.logn, inverse, a, s);
     }
 }
 

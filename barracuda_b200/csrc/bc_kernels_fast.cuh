@@ -443,16 +443,22 @@ struct Coop {
     }
 
     // Multiplies the CTA's share of the working array, coefficient-wise mod
-    // q, by `src` (canonical residues in this stage's order): the pointwise
-    // product of a fused polynomial multiplication.
-    __device__ __forceinline__ static void mul(W *smem, const uint64_t *src, uint32_t rank,
-                                               const LimbConst &lc) {
+    // q, by `src` (in this stage's order): the pointwise product of a fused
+    // polynomial multiplication or transform-and-multiply.  `src` words are
+    // reduced first (any u64 for 64-bit words; words >= 2^32 set `bad` for
+    // 32-bit words, as the input loads do).  Kept out of line: inlined next
+    // to a transform under the 64-register budget, it made the kernels
+    // spill 460-550 bytes per thread inside the passes (ptxas -v); as a call
+    // they spill at most 12.
+    __device__ __noinline__ static void mul(W *smem, const uint64_t *src, uint32_t rank,
+                                            const LimbConst &lc, uint32_t &bad) {
         const uint32_t tid = threadIdx.x;
         const uint32_t kr = NAT ? rank_pos<S>(rank, PHASE) : (__brev(rank_pos<S>(rank, PHASE)) >> (32 - L));
         const uint32_t kt = natural_of<S, L>(2 * tid, PHASE, NAT) + kr;
         const uint32_t at = smem_of_natural<S, L>(natural_of<S, L>(2 * tid, PHASE, NAT), PHASE, NAT);
         constexpr uint32_t a1 = smem_of_natural<S, L>(natural_of<S, L>(1, PHASE, NAT), PHASE, NAT);
         constexpr int kBatch = A::kBits == 32 ? 8 : 4;
+        const W q = static_cast<W>(lc.q), one_q = static_cast<W>(lc.one_shoup);
 #pragma unroll
         for (int j0 = 0; j0 < kIters; j0 += kBatch) {
             ulonglong2 x[kBatch];
@@ -464,8 +470,8 @@ struct Coop {
             for (int j = 0; j < kBatch && j0 + j < kIters; ++j) {
                 const uint32_t a0 = at + smem_of_natural<S, L>(natural_of<S, L>(2 * (j0 + j) * T, PHASE, NAT),
                                                                PHASE, NAT);
-                smem[a0] = mulmod_lc(smem[a0], static_cast<W>(x[j].x), lc);
-                smem[a0 + a1] = mulmod_lc(smem[a0 + a1], static_cast<W>(x[j].y), lc);
+                smem[a0] = mulmod_lc(smem[a0], A::load_reduce(x[j].x, q, one_q, bad), lc);
+                smem[a0 + a1] = mulmod_lc(smem[a0 + a1], A::load_reduce(x[j].y, q, one_q, bad), lc);
             }
         }
     }
@@ -739,7 +745,7 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, fal
     Fwd::prefetch(ring_f, tw, rank);
     __syncthreads();
     Fwd::run(work, tw, lc, rank, ring_f);  // ends with the working array complete
-    Mid::mul(work, a.in2 + base, rank, lc);
+    Mid::mul(work, a.in2 + base, rank, lc, bad);
     typename Inv::Ring ring_i;
     Inv::prefetch(ring_i, tw2, rank);
     __syncthreads();
@@ -748,6 +754,92 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, fal
     if constexpr (A::kBits == 32) {
         if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) atomicOr(a.status, kStatusInputRange);
     }
+}
+
+// Transform and pointwise product fused in one kernel, one cluster per
+// (limb, polynomial), negacyclic plans:
+//   INV = false: C = NTT(A) * B^, the product in the forward's epilogue;
+//   INV = true:  C = INTT(A^ * B^), the product in the inverse's prologue.
+// A^, B^ and the forward's C are in natural order.  B^ is read in the
+// working array's order at the one point where the values sit in that order
+// (after the forward passes, before the inverse passes), as in the fused
+// polynomial product.  HBM sees 24N bytes per polynomial instead of the 32N
+// of a transform launch followed by a pointwise launch.  C may alias A or
+// B^: each CTA reads B^ (forward) exactly where it then writes C, and reads
+// A^ and B^ (inverse) before the phase-change barrier that precedes every
+// store.
+template <class A, int L, int LOGE, bool INV>
+__global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, false>::kMinBlocks))
+    k_ntt_mul_fast(KArgs a) {
+    using W = typename A::W;
+    using Sh = Shape<L, LOGE>;
+    using S = Sched<L, LOGE>;
+    using Tr = Step<A, L, LOGE, INV, INV, 0>;  // negacyclic: CT forward, GS inverse with N^-1 folded
+    constexpr int ph_in = S::pass(pass_at<S, INV>(0)).phase;
+    constexpr int ph_out = S::pass(pass_at<S, INV>(S::kPasses - 1)).phase;
+    using In = Coop<A, S, L, Sh::kT, Sh::kLocal, ph_in, !INV>;
+    using Out = Coop<A, S, L, Sh::kT, Sh::kLocal, ph_out, INV>;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    W *work = reinterpret_cast<W *>(smem_raw);
+    const uint32_t rank = Sh::kC > 1 ? cluster_rank() : 0u;
+    const uint64_t cl = blockIdx.x / Sh::kC;
+    const uint64_t limb = cl / a.batch, poly = cl % a.batch;
+    const int64_t base = static_cast<int64_t>(limb) * a.limb_stride + static_cast<int64_t>(poly) * a.poly_stride;
+    const LimbConst &lc = a.limbs[limb];
+    const typename A::Tw *tw = reinterpret_cast<const typename A::Tw *>(a.tw) + (limb << L);
+    uint32_t bad = 0;
+    In::load(work, a.in + base, rank, lc, bad);
+    // the thread multiplies the words it has just written: no barrier needed
+    if constexpr (INV) In::mul(work, a.in2 + base, rank, lc, bad);
+    typename Tr::Ring ring;
+    Tr::prefetch(ring, tw, rank);
+    __syncthreads();
+    Tr::run(work, tw, lc, rank, ring);  // ends with the working array complete
+    if constexpr (!INV) Out::mul(work, a.in2 + base, rank, lc, bad);
+    Out::store(work, a.out + base, rank, lc);
+    if constexpr (A::kBits == 32) {
+        if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) atomicOr(a.status, kStatusInputRange);
+    }
+}
+
+// One cluster of Shape<L, LOGE>::kC CTAs per (limb, polynomial).
+template <class A, int L, int LOGE>
+int launch_per_poly(void (*kern)(KArgs), bool *attr_set, const char *name, const KArgs &a, cudaStream_t s) {
+    using Sh = Shape<L, LOGE>;
+    const size_t smem = Smem<A, L, LOGE, false>::kBytes;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return cuda_fail(e, format("%s shared-memory attribute", name).c_str());
+        if (Sh::kC > 8) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return cuda_fail(e, format("%s cluster-size attribute", name).c_str());
+        }
+        if (dev < 64) attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(Sh::kT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = Sh::kC;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = Sh::kC > 1 ? 1 : 0;
+    const uint64_t polys = static_cast<uint64_t>(a.batch) * a.n_limbs;
+    cfg.gridDim = dim3(static_cast<unsigned>(polys * Sh::kC));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+    if (e != cudaSuccess) return cuda_fail(e, format("%s launch", name).c_str());
+    return BC_OK;
+}
+
+template <class A, int L, int LOGE, bool INV>
+int launch_ntt_mul_one(const KArgs &a, cudaStream_t s) {
+    static bool attr_set[64] = {false};
+    return launch_per_poly<A, L, LOGE>(k_ntt_mul_fast<A, L, LOGE, INV>, attr_set, "k_ntt_mul_fast", a, s);
 }
 
 template <class A, int L, int LOGE>
@@ -817,6 +909,30 @@ template <class A, int V, int L>
 int polymul_if(const KArgs &a, cudaStream_t s) {
     if constexpr (sched_logc(L, V) >= 0) return launch_polymul_one<A, L, V>(a, s);
     return fail(BC_ERR_INTERNAL, format("no fast schedule for log2 N = %d, variant %d", L, V));
+}
+
+template <class A, int V, int L>
+int ntt_mul_if(bool inverse, const KArgs &a, cudaStream_t s) {
+    if constexpr (sched_logc(L, V) >= 0)
+        return inverse ? launch_ntt_mul_one<A, L, V, true>(a, s) : launch_ntt_mul_one<A, L, V, false>(a, s);
+    return fail(BC_ERR_INTERNAL, format("no fast schedule for log2 N = %d, variant %d", L, V));
+}
+
+// Transform fused with a pointwise product (see k_ntt_mul_fast).
+template <class A, int V>
+int dispatch_ntt_mul_l(uint32_t L, bool inverse, const KArgs &a, cudaStream_t s) {
+    switch (L) {
+    case 10: return ntt_mul_if<A, V, 10>(inverse, a, s);
+    case 11: return ntt_mul_if<A, V, 11>(inverse, a, s);
+    case 12: return ntt_mul_if<A, V, 12>(inverse, a, s);
+    case 13: return ntt_mul_if<A, V, 13>(inverse, a, s);
+    case 14: return ntt_mul_if<A, V, 14>(inverse, a, s);
+    case 15: return ntt_mul_if<A, V, 15>(inverse, a, s);
+    case 16: return ntt_mul_if<A, V, 16>(inverse, a, s);
+    case 17: return ntt_mul_if<A, V, 17>(inverse, a, s);
+    default: break;
+    }
+    return fail(BC_ERR_INTERNAL, format("no fast schedule for log2 N = %u", L));
 }
 
 // Fused polymul for the fast sizes (see k_polymul_fast).

@@ -15,13 +15,6 @@
 namespace bc {
 namespace {
 
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit_wait_all() {
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
-
 // 32-bit shared::cluster address of the word at local shared address `saddr`
 // in the shared memory of cluster CTA `rank`, and a store to it.
 __device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) {
@@ -204,32 +197,31 @@ __global__ void __launch_bounds__(kClusterThreads, 2)
                 const uint64_t x = buf[u & (B - 1)];
                 __stcs(dst + static_cast<size_t>(jh) * C, (u & B) ? negate_mod(x, q) : x);
             }
-            cluster_sync_relaxed();
-            continue;
-        }
-        // 2. permute within the class (into registers) ...
-        uint64_t v[kPer];
+        } else {
+            // 2. permute within the class (into registers) ...
+            uint64_t v[kPer];
 #pragma unroll
-        for (uint32_t k = 0; k < kPer; ++k) {
-            const uint32_t jh = k * T + threadIdx.x;
-            const uint32_t u = (kappa + jh * ginv) & (2 * B - 1);
-            const uint64_t x = buf[u & (B - 1)];
-            v[k] = (u & B) ? negate_mod(x, q) : x;
-        }
-        cl.sync();
-        // ... and send each output word to the CTA that stores its block
+            for (uint32_t k = 0; k < kPer; ++k) {
+                const uint32_t jh = k * T + threadIdx.x;
+                const uint32_t u = (kappa + jh * ginv) & (2 * B - 1);
+                const uint64_t x = buf[u & (B - 1)];
+                v[k] = (u & B) ? negate_mod(x, q) : x;
+            }
+            cl.sync();
+            // ... and send each output word to the CTA that stores its block
 #pragma unroll
-        for (uint32_t k = 0; k < kPer; ++k) {
-            const uint32_t jh = k * T + threadIdx.x;
-            st_cluster_u64(cluster_addr(sbuf + 8 * (jl * kStride + jh % kCol), jh / kCol), v[k]);
-        }
-        cl.sync();
-        // 3. output block, coalesced
-        uint64_t *dst = a.out + base;
+            for (uint32_t k = 0; k < kPer; ++k) {
+                const uint32_t jh = k * T + threadIdx.x;
+                st_cluster_u64(cluster_addr(sbuf + 8 * (jl * kStride + jh % kCol), jh / kCol), v[k]);
+            }
+            cl.sync();
+            // 3. output block, coalesced
+            uint64_t *dst = a.out + base;
 #pragma unroll 4
-        for (uint32_t k = 0; k < kPer; ++k) {
-            const uint32_t p = k * T + threadIdx.x;
-            __stcs(dst + p, buf[(p & (C - 1)) * kStride + (p >> LOGC)]);
+            for (uint32_t k = 0; k < kPer; ++k) {
+                const uint32_t p = k * T + threadIdx.x;
+                __stcs(dst + p, buf[(p & (C - 1)) * kStride + (p >> LOGC)]);
+            }
         }
         cluster_sync_relaxed();
     }

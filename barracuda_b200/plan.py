@@ -105,6 +105,16 @@ class NttPlan:
         check(lib().bc_pointwise_mul(self.handle, _ptr(a), _ptr(b), _ptr(c), batch,
                                      self._layout(layout), stream or None))
 
+    def forward_mul(self, a, b_hat, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
+        """C = NTT(A) * B^ (one fused launch on negacyclic plans)."""
+        check(lib().bc_ntt_forward_mul(self.handle, _ptr(a), _ptr(b_hat), _ptr(c), batch,
+                                       self._layout(layout), stream or None))
+
+    def inverse_mul(self, a_hat, b_hat, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
+        """C = INTT(A^ * B^) (one fused launch on negacyclic plans)."""
+        check(lib().bc_ntt_inverse_mul(self.handle, _ptr(a_hat), _ptr(b_hat), _ptr(c), batch,
+                                       self._layout(layout), stream or None))
+
     def poly_add(self, a, b, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
         check(lib().bc_poly_add(self.handle, _ptr(a), _ptr(b), _ptr(c), batch, self._layout(layout),
                                 stream or None))

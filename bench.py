@@ -568,6 +568,10 @@ KERNEL_CASES = {
     "pointwise": (16, 16, "k_pointwise", 24),
     "modulus_switch": (16, 16, "k_modulus_switch", 16),
     "decompose": (16, 16, "k_decompose", 32),            # base 2^16, 3 digits
+    "forward": (16, 16, "k_ntt_fast", 16),               # the transform alone, for comparison
+    "inverse": (16, 16, "k_ntt_fast", 16),
+    "forward_mul": (16, 16, "k_ntt_mul_fast", 24),       # C = NTT(A) * B^
+    "inverse_mul": (16, 16, "k_ntt_mul_fast", 24),       # C = INTT(A^ * B^)
 }
 
 
@@ -606,6 +610,10 @@ def run_kernel_case(args):
         "pointwise": lambda: plan.pointwise_mul(a, b, c, batch, stream=sh),
         "modulus_switch": lambda: bc.modulus_switch(dev, a, c, words, qs[0], qs[1] >> 8, stream=sh),
         "decompose": lambda: bc.decompose(dev, a, c, words, 1 << 16, 3, stream=sh),
+        "forward": lambda: plan.forward(a, c, batch, stream=sh),
+        "inverse": lambda: plan.inverse(a, c, batch, stream=sh),
+        "forward_mul": lambda: plan.forward_mul(a, b, c, batch, stream=sh),
+        "inverse_mul": lambda: plan.inverse_mul(a, b, c, batch, stream=sh),
     }
     fn = ops[case]
     for _ in range(args.warmup):

@@ -251,6 +251,21 @@ int bc_poly_sub(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_
                 uint32_t batch, const bc_layout *layout, void *stream);
 int bc_poly_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                 uint32_t batch, const bc_layout *layout, void *stream);
+/* Transform fused with the pointwise product:
+ *   bc_ntt_forward_mul: C = NTT(A) * B^, the product in the forward's epilogue;
+ *   bc_ntt_inverse_mul: C = INTT(A^ * B^), the product in the inverse's prologue.
+ * A^, B^ and the forward's result use bc_ntt_forward's natural order.  B^
+ * words are reduced mod q_l first (a word >= 2^32 given to a plan whose moduli
+ * are below 2^31 is reported as BC_ERR_INVALID_INPUT at the next
+ * bc_ctx_sync, as for the transforms' inputs).  On BC_NTT_NEGACYCLIC plans
+ * with the cluster kernels (16-byte aligned operands, even strides) this is
+ * one launch moving 24N bytes per polynomial; other plans and layouts run a
+ * transform launch and a pointwise launch, with the same result.  C may alias
+ * A or B^. */
+int bc_ntt_forward_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b_hat, uint64_t *d_c,
+                       uint32_t batch, const bc_layout *layout, void *stream);
+int bc_ntt_inverse_mul(bc_plan *plan, const uint64_t *d_a_hat, const uint64_t *d_b_hat,
+                       uint64_t *d_c, uint32_t batch, const bc_layout *layout, void *stream);
 /* C = A * B mod q_l, coefficient-wise. */
 int bc_pointwise_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                      uint32_t batch, const bc_layout *layout, void *stream);

@@ -286,6 +286,114 @@ def test_plan_strided_ciphertext_layout_and_in_place(device):
     assert (buf.to_u64() == x).all()
 
 
+@pytest.mark.parametrize("logn,bits", [(10, 31), (12, 31), (14, 31), (15, 60), (16, 31), (17, 31), (16, 60)])
+def test_forward_mul_and_inverse_mul_match_chains(device, logn, bits):
+    """C = NTT(A) * B^ and C = INTT(A^ * B^) in one launch equal the
+    transform-then-pointwise chains; aliasing C with either input."""
+    n, limbs, batch = 1 << logn, 2, 3
+    plan, qs, _ = _plan(device, n, limbs, bits, bc.NEGACYCLIC)
+    total = limbs * batch * n
+    a, b, bh, t, c = (_alloc(device, total) for _ in range(5))
+    plan.fill_uniform(a, batch, seed=3)
+    plan.fill_uniform(b, batch, seed=4)
+    plan.forward(b, bh, batch)                  # B^ = NTT(B)
+    plan.forward(a, t, batch)
+    plan.pointwise_mul(t, bh, t, batch)         # chain: NTT(A) * B^
+    plan.forward_mul(a, bh, c, batch)
+    device.synchronize()
+    want_f = t.to_u64().copy()
+    assert (c.to_u64() == want_f).all()
+    plan.pointwise_mul(bh, bh, t, batch)        # chain: INTT(B^ * B^)
+    plan.inverse(t, t, batch)
+    plan.inverse_mul(bh, bh, c, batch)
+    device.synchronize()
+    want_i = t.to_u64().copy()
+    assert (c.to_u64() == want_i).all()
+    # in place: C = A, then C = B^
+    x = _alloc(device, total)
+    plan.fill_uniform(x, batch, seed=3)
+    plan.forward_mul(x, bh, x, batch)
+    device.synchronize()
+    assert (x.to_u64() == want_f).all()
+    y = _alloc(device, total)
+    plan.forward(b, y, batch)
+    plan.forward_mul(a, y, y, batch)
+    device.synchronize()
+    assert (y.to_u64() == want_f).all()
+    plan.forward(b, y, batch)
+    plan.inverse_mul(y, y, y, batch)
+    device.synchronize()
+    assert (y.to_u64() == want_i).all()
+    plan.close()
+
+
+def test_forward_mul_inverse_mul_compose_to_polymul(device):
+    """INTT(NTT(A) * NTT(B)) through the fused forward equals bc_polymul and
+    the oracle's negacyclic convolution."""
+    n, limbs, batch = 1 << 10, 2, 2
+    plan, qs, _ = _plan(device, n, limbs, 31, bc.NEGACYCLIC)
+    total = limbs * batch * n
+    a, b, bh, c, want = (_alloc(device, total) for _ in range(5))
+    plan.fill_uniform(a, batch, seed=8)
+    plan.fill_uniform(b, batch, seed=9)
+    plan.forward(b, bh, batch)
+    plan.forward_mul(a, bh, c, batch)
+    plan.inverse(c, c, batch)
+    plan.polymul(a, b, want, batch)
+    device.synchronize()
+    C, W, A, B = c.to_u64(), want.to_u64(), a.to_u64(), b.to_u64()
+    assert (C == W).all()
+    assert (C[:n] == O.negacyclic_convolution(A[:n], B[:n], n, qs[0])).all()
+    plan.close()
+
+
+def test_forward_mul_fallbacks_and_wide_words(device):
+    """B^ words in [q, 2^32) are reduced first; odd strides and cyclic plans
+    take the two-launch path with the same result."""
+    n, limbs, batch = 1 << 12, 2, 2
+    plan, qs, _ = _plan(device, n, limbs, 31, bc.NEGACYCLIC)
+    rng = np.random.default_rng(5)
+    total = limbs * batch * n
+    A = rng.integers(0, qs[-1], total, dtype=np.uint64)
+    Bh = rng.integers(0, 2**32, total, dtype=np.uint64)   # not reduced
+    a, bh, c = upload(device, A), upload(device, Bh), _alloc(device, total)
+    plan.forward_mul(a, bh, c, batch)
+    X = _alloc(device, total)
+    plan.forward(a, X, batch)
+    device.synchronize()
+    Xh, C = X.to_u64(), c.to_u64()
+    for l in range(limbs):
+        for p in range(batch):
+            o = (l * batch + p) * n
+            assert (C[o:o + n] == O.exact_poly_mul(Xh[o:o + n], Bh[o:o + n], qs[l])).all(), (l, p)
+    # odd poly stride: [limb][poly] with a one-word gap, not 16-byte aligned
+    lay = bc.Layout(limb_stride=batch * (n + 1), poly_stride=n + 1)
+    big = limbs * batch * (n + 1)
+    a2, b2, c2, t2 = (_alloc(device, big) for _ in range(4))
+    plan.fill_uniform(a2, batch, seed=1, layout=lay)
+    plan.fill_uniform(b2, batch, seed=2, layout=lay)
+    plan.forward_mul(a2, b2, c2, batch, layout=lay)
+    plan.forward(a2, t2, batch, layout=lay)
+    plan.pointwise_mul(t2, b2, t2, batch, layout=lay)
+    device.synchronize()
+    C2, T2 = c2.to_u64(), t2.to_u64()
+    for l in range(limbs):
+        for p in range(batch):
+            o = l * batch * (n + 1) + p * (n + 1)
+            assert (C2[o:o + n] == T2[o:o + n]).all(), (l, p)
+    plan.close()
+    cplan, _, _ = _plan(device, n, limbs, 31, bc.CYCLIC)
+    a3, b3, c3, t3 = (_alloc(device, total) for _ in range(4))
+    cplan.fill_uniform(a3, batch, seed=1)
+    cplan.fill_uniform(b3, batch, seed=2)
+    cplan.inverse_mul(a3, b3, c3, batch)
+    cplan.pointwise_mul(a3, b3, t3, batch)
+    cplan.inverse(t3, t3, batch)
+    device.synchronize()
+    assert (c3.to_u64() == t3.to_u64()).all()
+    cplan.close()
+
+
 def _exact_negacyclic(x, n, q, psi):
     """Exact O(N log N) negacyclic forward transform of one polynomial (oracle)."""
     _, out = O.baseline_run("exact_negacyclic_ntt", x, n, [q], [psi], 1)
