@@ -164,8 +164,10 @@ struct Arith64 {
     // Exact a*b mod q for a, b < 4q (q < 2^62, k = bit length of q):
     // Barrett with mu = floor(2^(2k) / q); quotient estimate within 2.
     __device__ __forceinline__ static W mulmod(W a, W b, W q, uint64_t mu, uint32_t k) {
-        a = sub_if(sub_if(a, 2 * q), q);
-        b = sub_if(sub_if(b, 2 * q), q);
+        return mulmod_reduced(sub_if(sub_if(a, 2 * q), q), sub_if(sub_if(b, 2 * q), q), q, mu, k);
+    }
+    // The same for a, b < q.
+    __device__ __forceinline__ static W mulmod_reduced(W a, W b, W q, uint64_t mu, uint32_t k) {
         const uint64_t lo = a * b, hi = __umul64hi(a, b);
         // t1 = floor(t / 2^(k-1)) fits in k+1 <= 63 bits
         const uint64_t t1 = (hi << (65 - k)) | (lo >> (k - 1));

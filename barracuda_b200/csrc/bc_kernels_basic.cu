@@ -310,6 +310,10 @@ __device__ __forceinline__ uint64_t reduce_any(uint64_t x, const CoeffConst &c) 
 }
 
 __device__ __forceinline__ uint64_t mulmod_any(uint64_t a, uint64_t b, const CoeffConst &c) {
+    if (a < c.q && b < c.q) {  // operands already reduced (the usual case): no pre-reduction
+        if (c.q <= 0xFFFFFFFFull) return reduce_any(a * b, c);
+        if (c.k <= 62) return Arith64::mulmod_reduced(a, b, c.q, c.mu, c.k);
+    }
     const uint64_t x = reduce_any(a, c), y = reduce_any(b, c);
     if (c.q <= 0xFFFFFFFFull) return reduce_any(x * y, c);  // x * y < 2^64
     if (c.k <= 62) return Arith64::mulmod(x, y, c.q, c.mu, c.k);
