@@ -38,10 +38,12 @@ int fast_variant(Word w, uint32_t logn, bool inverse) {
     const int L = static_cast<int>(logn);
     const int e = inverse ? (env_inv ? env_inv : env_all) : (env_fwd ? env_fwd : env_all);
     if (e && fast::sched_logc(L, e) >= 0) return e;
-    // Measured on B200 (forward and inverse, ~2 GiB batches): 16 per thread
-    // wins for N <= 2^12, 256-thread CTAs of 32 per thread for 2^14..2^17
-    // (clusters of 16 at 2^17); 128-thread CTAs (7) lose at 2^16.
-    if (L <= 12) return 4;
+    // Measured on B200 (forward and inverse, ~2 GiB batches): 32 per thread
+    // in one CTA of up to 2^13 words (5) wins for N <= 2^13 (0.90 of HBM at
+    // 2^12 against 0.80 for 16 per thread, whose loads and stores stay
+    // inlined), 256-thread CTAs of 32 per thread for 2^14..2^17 (clusters of
+    // 16 at 2^17); 128-thread CTAs (7) lose at 2^16.
+    if (L <= 13 && fast::sched_logc(L, 5) >= 0) return 5;
     if (fast::sched_logc(L, 6) >= 0) return 6;
     return 5;
 }
