@@ -338,14 +338,19 @@ namespace {
 // How run_polymul computes a product (see there).
 enum class PolymulPath { Smem, Fast, Unfused };
 
+// The cluster kernels' product (NTT(B) into C, then one fused launch) comes
+// first wherever it applies: measured on B200 (32 limbs, 2^25 words per
+// operand) it is 2.5-3.7x faster than the single-CTA shared-memory kernel at
+// N = 2^10..2^14, which serves cyclic plans and the layouts the cluster
+// kernels cannot take.
 PolymulPath polymul_path(const bc_plan *p, const KArgs &a) {
-    if (p->logn >= 1 && p->logn <= polymul_smem_max_logn(p->word)) return PolymulPath::Smem;
     const auto aligned = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     const bool all_alias = a.in == a.out && a.in2 == a.out;
     if (p->mode == BC_NTT_NEGACYCLIC && p->kind == KernelKind::Cluster && fast_layout_ok(a) &&
         aligned(a.in2) && !all_alias &&
         fast_variant_for(p->word, p->logn, false) == fast_variant_for(p->word, p->logn, true))
         return PolymulPath::Fast;
+    if (p->logn >= 1 && p->logn <= polymul_smem_max_logn(p->word)) return PolymulPath::Smem;
     return PolymulPath::Unfused;
 }
 

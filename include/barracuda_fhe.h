@@ -269,16 +269,16 @@ int bc_ntt_inverse_mul(bc_plan *plan, const uint64_t *d_a_hat, const uint64_t *d
 /* C = A * B mod q_l, coefficient-wise. */
 int bc_pointwise_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                      uint32_t batch, const bc_layout *layout, void *stream);
-/* C = INTT(NTT(A) * NTT(B)) per (limb, polynomial).  Up to N = 2^14
- * (moduli below 2^31) or 2^13 (wider moduli): one fused kernel.  Above that,
- * negacyclic plans on the cluster kernels (16-byte aligned operands, even
- * strides, not A == B == C) run two launches: NTT(B) into C, then one fused
- * kernel C = INTT(NTT(A) * C); nothing is allocated.  Every other case
- * (cyclic plans above the fused size, other layouts) transforms both
- * operands into a temporary device buffer, multiplies and runs the inverse
- * into C, needing the default layout (layout NULL or compact); that
- * temporary is allocated, the stream synchronized and the buffer freed on
- * every call. */
+/* C = INTT(NTT(A) * NTT(B)) per (limb, polynomial).  Negacyclic plans on
+ * the cluster kernels (N >= 2^10, 16-byte aligned operands, even strides, not
+ * A == B == C) run two launches: NTT(B) into C, then one fused kernel
+ * C = INTT(NTT(A) * C).  Otherwise, up to N = 2^14 (moduli below 2^31) or
+ * 2^13 (wider moduli), one fused shared-memory kernel.  Neither allocates.
+ * Every other case (cyclic plans above the fused size, other layouts)
+ * transforms both operands into a temporary device buffer, multiplies and
+ * runs the inverse into C, needing the default layout (layout NULL or
+ * compact); that temporary is allocated, the stream synchronized and the
+ * buffer freed on every call. */
 int bc_polymul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                uint32_t batch, const bc_layout *layout, void *stream);
 

@@ -394,6 +394,27 @@ def test_forward_mul_fallbacks_and_wide_words(device):
     cplan.close()
 
 
+@pytest.mark.parametrize("logn", [10, 12, 14])
+def test_polymul_shared_memory_path_for_odd_strides(device, logn):
+    """Layouts the cluster kernels cannot take (odd strides) route negacyclic
+    products to the single-CTA shared-memory kernel: same result as the
+    schoolbook negacyclic convolution."""
+    n, limbs, batch = 1 << logn, 2, 2
+    plan, qs, _ = _plan(device, n, limbs, 31, bc.NEGACYCLIC)
+    lay = bc.Layout(limb_stride=batch * (n + 1), poly_stride=n + 1)
+    big = limbs * batch * (n + 1)
+    a, b, c = (_alloc(device, big) for _ in range(3))
+    plan.fill_uniform(a, batch, seed=21, layout=lay)
+    plan.fill_uniform(b, batch, seed=22, layout=lay)
+    plan.polymul(a, b, c, batch, layout=lay)
+    device.synchronize()
+    A, B, C = a.to_u64(), b.to_u64(), c.to_u64()
+    for l, p in ((0, 0), (1, 1)):
+        o = l * batch * (n + 1) + p * (n + 1)
+        assert (C[o:o + n] == O.negacyclic_convolution(A[o:o + n], B[o:o + n], n, qs[l])).all(), (l, p)
+    plan.close()
+
+
 def _exact_negacyclic(x, n, q, psi):
     """Exact O(N log N) negacyclic forward transform of one polynomial (oracle)."""
     _, out = O.baseline_run("exact_negacyclic_ntt", x, n, [q], [psi], 1)
