@@ -158,13 +158,24 @@ uint64_t orc_digest(const uint64_t *x, size_t count, uint64_t first_index);
 /* ---------------- part 3: threaded CPU baseline ---------------- */
 
 /* Runs orc_ref_ntt (kind 0), orc_ref_intt (kind 1), orc_ref_negacyclic_ntt (2),
- * orc_ref_negacyclic_intt (3) or an exact O(N log N) negacyclic forward (4) on
+ * orc_ref_negacyclic_intt (3), an exact O(N log N) negacyclic forward (4) or
+ * inverse (5) on
  * `count` polynomials of `degree` coefficients stored back to back, using up
  * to `threads` POSIX threads.  Polynomial p uses modulus moduli[p % n_moduli]
  * and root roots[p % n_moduli].  Returns the wall time in seconds. */
 double orc_baseline_run(int kind, const uint64_t *in, uint64_t *out, uint32_t degree,
                         uint32_t count, const uint64_t *moduli, const uint64_t *roots,
                         uint32_t n_moduli, int threads);
+
+/* Polynomial products c = a * b of `count` limb-polynomial pairs stored back
+ * to back, on up to `threads` threads; pair p uses moduli[p % n_moduli] and
+ * roots[p % n_moduli].  kind 0: the reference's cyclic FheFastPolyMul chain
+ * (root = omega); 1: the reference ops chained into a negacyclic product
+ * (root = psi); 2: exact negacyclic product (psi); 3: exact cyclic product
+ * (omega).  Returns the wall time in seconds. */
+double orc_batch_polymul(int kind, const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t degree,
+                         uint32_t count, const uint64_t *moduli, const uint64_t *roots, uint32_t n_moduli,
+                         int threads);
 
 #ifdef __cplusplus
 }

@@ -96,6 +96,8 @@ def lib():
             "orc_decompose": (None, [_u64p, _u64p, ctypes.c_size_t, u32, u32]),
             "orc_baseline_run": (ctypes.c_double,
                                  [i32, _u64p, _u64p, u32, u32, _u64p, _u64p, u32, i32]),
+            "orc_batch_polymul": (ctypes.c_double,
+                                  [i32, _u64p, _u64p, _u64p, u32, u32, _u64p, _u64p, u32, i32]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -287,7 +289,8 @@ def __getattr__(name):
 
 
 BASELINE_KIND = {"ntt": 0, "intt": 1, "negacyclic_ntt": 2, "negacyclic_intt": 3,
-                 "exact_negacyclic_ntt": 4}
+                 "exact_negacyclic_ntt": 4, "exact_negacyclic_intt": 5}
+POLYMUL_KIND = {"ref_cyclic": 0, "ref_negacyclic": 1, "exact_negacyclic": 2, "exact_cyclic": 3}
 
 
 def baseline_run(kind, x, degree, moduli, roots, threads):
@@ -299,3 +302,24 @@ def baseline_run(kind, x, degree, moduli, roots, threads):
     secs = lib().orc_baseline_run(BASELINE_KIND[kind], _p(x), _p(out), degree, count,
                                   _p(m), _p(r), m.size, threads)
     return secs, out
+
+
+def _threads(threads):
+    return threads if threads else (os.cpu_count() or 1)
+
+
+def batch_transform(kind, x, degree, moduli, roots, threads=None):
+    """`kind` (a BASELINE_KIND name) of each limb-polynomial of x (back to back);
+    polynomial p uses moduli[p] and roots[p].  Multi-threaded."""
+    return baseline_run(kind, x, degree, moduli, roots, _threads(threads))[1]
+
+
+def batch_polymul(kind, a, b, degree, moduli, roots, threads=None):
+    """Products of the limb-polynomial pairs of a and b (back to back); pair p
+    uses moduli[p] and roots[p]; `kind` is a POLYMUL_KIND name.  Multi-threaded."""
+    a, b = _arr(a), _arr(b)
+    c = np.zeros_like(a)
+    m, r = _arr(moduli), _arr(roots)
+    lib().orc_batch_polymul(POLYMUL_KIND[kind], _p(a), _p(b), _p(c), degree, a.size // degree,
+                            _p(m), _p(r), m.size, _threads(threads))
+    return c

@@ -1,14 +1,17 @@
 """Parity of the CUDA path on the five benchmark configurations at their full
 sizes, through the C ABI.
 
-At full size every limb-polynomial is checked through size-independent
-properties: the round trip is the identity (digests of the whole batch), and
-for products NTT(c) = NTT(a) * NTT(b).  A few sampled limb-polynomials per
-config are checked value by value against the oracle: the reference's own
-algorithm (oracle/ref_wgsl.c) for moduli below 2^31, exact u128 arithmetic for
-the 60-bit family, where the reference truncates its products.  Inputs are
-the seeded uniform values of bc_fill_uniform, regenerated on the host by the
-oracle for the samples.  Bar: bit-exact."""
+At full size every limb-polynomial is checked through a size-independent
+property: the round trip is the identity (digests of the whole batch).  Every
+limb is also checked value by value against the oracle, on the first and the
+last polynomial of the batch and on one in between: the forward transform of
+the seeded input, and the inverse transform applied to a fresh input (not only
+through the round trip, which could hide an error the inverse undoes).  The
+oracle is the reference's own algorithm (oracle/ref_wgsl.c) for moduli below
+2^31 and exact u128 arithmetic for the 60-bit family, where the reference
+truncates its products; it runs on all host threads.  Inputs are the seeded
+uniform values of bc_fill_uniform, regenerated on the host by the oracle.
+Bar: bit-exact."""
 import numpy as np
 import pytest
 import torch
@@ -53,8 +56,27 @@ def stream():
     torch.cuda.set_stream(prev)
 
 
-def _batch_case(device, stream, n, limbs, batch, bits, lay_kind, samples, seed=0):
-    """Fills, forwards, samples, inverses; returns nothing, asserts parity."""
+def _gather(t, offs, n):
+    """The limb-polynomials at word offsets `offs` of device tensor t, back to back (host)."""
+    return np.concatenate([_host(t, o, n) for o in offs])
+
+
+def _limb_samples(limbs, batch, rng, every_poly_ends=True):
+    """(limb, poly) pairs: every limb on the first and last polynomial and on
+    one polynomial in between (every limb once when every_poly_ends is False)."""
+    pairs = []
+    for l in range(limbs):
+        mid = int(rng.integers(batch))
+        pairs.append((l, mid))
+        if every_poly_ends:
+            pairs.extend([(l, 0), (l, batch - 1)])
+    return sorted(set(pairs))
+
+
+def _batch_case(device, stream, n, limbs, batch, bits, lay_kind, every_poly_ends=True, seed=0):
+    """Fills, forwards and inverses a full batch; asserts every sampled limb-
+    polynomial against the oracle (forward of the input, inverse of a fresh
+    input) and the whole-batch round trip by digest."""
     sh = stream.cuda_stream
     qs = bc.ntt_primes(bits, n, limbs)
     psis = _roots(qs, n, bc.NEGACYCLIC)
@@ -67,20 +89,33 @@ def _batch_case(device, stream, n, limbs, batch, bits, lay_kind, samples, seed=0
         off = lambda l, p: (p * limbs + l) * n  # noqa: E731
     words = limbs * batch * n
     x = torch.empty(words, dtype=torch.int64, device="cuda")
-    y = torch.empty_like(x)
+    y, z = torch.empty_like(x), torch.empty_like(x)
     plan.fill_uniform(x, batch, seed=seed, layout=lay, stream=sh)
     d_in = _digest(device, x, words, sh)
     plan.forward(x, y, batch, layout=lay, stream=sh)
+    plan.inverse(x, z, batch, layout=lay, stream=sh)  # a fresh input for the inverse
     torch.cuda.synchronize()
     rng = np.random.default_rng(n + limbs + bits)
-    for _ in range(samples):
-        l, p = int(rng.integers(limbs)), int(rng.integers(batch))
-        xin = _host(x, off(l, p), n)
-        # the device generator is the oracle's counter-based generator
-        g0 = (l * batch + p) * n
-        assert (xin == O.seeded_fill(n, seed, g0, qs[l])).all(), (n, l, p)
-        want = _forward_oracle(xin, n, qs[l], psis[l], bits, bc.NEGACYCLIC)
-        assert (_host(y, off(l, p), n) == want).all(), (n, bits, l, p)
+    pairs = _limb_samples(limbs, batch, rng, every_poly_ends)
+    assert {l for l, _ in pairs} == set(range(limbs))
+    offs = [off(l, p) for l, p in pairs]
+    xin = _gather(x, offs, n)
+    # the device generator is the oracle's counter-based generator
+    for k, (l, p) in enumerate(pairs[:4] + pairs[-4:]):
+        kk = pairs.index((l, p))
+        assert (xin[kk * n:(kk + 1) * n] == O.seeded_fill(n, seed, (l * batch + p) * n, qs[l])).all(), (n, l, p)
+    mods = [qs[l] for l, _ in pairs]
+    roots = [psis[l] for l, _ in pairs]
+    fwd_kind, inv_kind = (("negacyclic_ntt", "negacyclic_intt") if bits == 31
+                          else ("exact_negacyclic_ntt", "exact_negacyclic_intt"))
+    want_f = O.batch_transform(fwd_kind, xin, n, mods, roots)
+    want_i = O.batch_transform(inv_kind, xin, n, mods, roots)
+    got_f, got_i = _gather(y, offs, n), _gather(z, offs, n)
+    for k, (l, p) in enumerate(pairs):
+        sl = slice(k * n, (k + 1) * n)
+        assert (got_f[sl] == want_f[sl]).all(), ("forward", n, bits, l, p)
+        assert (got_i[sl] == want_i[sl]).all(), ("inverse", n, bits, l, p)
+    del z
     plan.inverse(y, y, batch, layout=lay, stream=sh)  # in place
     assert _digest(device, y, words, sh) == d_in, "round trip is not the identity"
     device.synchronize()
@@ -119,31 +154,35 @@ def test_config0_single_roundtrip_n4096(device, stream, bits):
 @pytest.mark.parametrize("bits", [60, 31])
 def test_config1_batched_forward_n2_14(device, stream, bits):
     """Config 1: N=2^14, 16 limbs x 64 polynomials, limb-major contiguous."""
-    _batch_case(device, stream, 1 << 14, 16, 64, bits, "limb_major", samples=4)
+    _batch_case(device, stream, 1 << 14, 16, 64, bits, "limb_major")
 
 
 @pytest.mark.parametrize("bits", [31, 60])
 def test_config3_ciphertext_batch_n2_16(device, stream, bits):
-    """Config 3: N=2^16, 48 limbs, 128 ciphertexts x 2 polynomials, [ct][2][limb][N]."""
-    _batch_case(device, stream, 1 << 16, 48, 256, bits, "ct_major", samples=3)
+    """Config 3: N=2^16, 48 limbs, 128 ciphertexts x 2 polynomials, [ct][2][limb][N].
+    Every limb of the first and the last ciphertext, and of one in between."""
+    _batch_case(device, stream, 1 << 16, 48, 256, bits, "ct_major")
 
 
 @pytest.mark.parametrize("logn", [12, 13, 14, 15, 16, 17])
 @pytest.mark.parametrize("bits", [60, 31])
 def test_config4_size_sweep(device, stream, logn, bits):
-    """Config 4: N in 2^12..2^17, 8 to 64 limbs, batch sized to about 2 GB (u64)."""
+    """Config 4: N in 2^12..2^17, 8 to 64 limbs, batch sized to about 2 GB (u64);
+    every limb checked once per N."""
     n = 1 << logn
     limbs = 64 if logn <= 13 else (16 if logn <= 15 else 8)
     batch = max(1, (2 << 30) // (8 * n * limbs))
-    _batch_case(device, stream, n, limbs, batch, bits, "limb_major", samples=1)
+    _batch_case(device, stream, n, limbs, batch, bits, "limb_major", every_poly_ends=False)
 
 
 @pytest.mark.parametrize("mode", [bc.NEGACYCLIC, bc.CYCLIC])
 @pytest.mark.parametrize("bits", [60, 31])
 def test_config2_polymul_n2_15(device, stream, mode, bits):
     """Config 2: NTT(a), NTT(b), pointwise, INTT at N=2^15, 32 limbs x 32 pairs.
-    Full batch: NTT(c) = NTT(a) * NTT(b) on samples, exact; for q < 2^31 the
-    sampled products also equal the reference's own NTT -> pointwise -> INTT chain."""
+    One pair of every limb is checked value by value: for q < 2^31 against the
+    reference's own chain (FheFastPolyMul for the cyclic mode, the ops chained
+    with a psi twist for the negacyclic one), for the 60-bit family against the
+    exact product."""
     n, limbs, batch = 1 << 15, 32, 32
     sh = stream.cuda_stream
     qs = bc.ntt_primes(bits, n, limbs)
@@ -157,21 +196,15 @@ def test_config2_polymul_n2_15(device, stream, mode, bits):
     plan.polymul(a, b, c, batch, stream=sh)
     torch.cuda.synchronize()
     rng = np.random.default_rng(bits + mode)
-    for _ in range(2):
-        l, p = int(rng.integers(limbs)), int(rng.integers(batch))
-        o = (l * batch + p) * n
-        A, B, C = _host(a, o, n), _host(b, o, n), _host(c, o, n)
-        q, r = qs[l], roots[l]
-        fwd = (lambda v: O.exact_negacyclic_ntt(v, n, q, r)) if mode == bc.NEGACYCLIC else \
-            (lambda v: O.exact_ntt(v, n, q, r))
-        FA, FB, FC = fwd(A), fwd(B), fwd(C)
-        prod = np.array([O.lib().orc_mulmod(int(u), int(v), q) for u, v in zip(FA, FB)], np.uint64)
-        assert (FC == prod).all(), (bits, mode, l, p)
-        if bits == 31:
-            if mode == bc.CYCLIC:
-                want = O.ref_fast_poly_mul(A, B, n, q, r)
-            else:
-                want = O.ref_negacyclic_intt(O.ref_pointwise(O.ref_negacyclic_ntt(A, n, q, r),
-                                                             O.ref_negacyclic_ntt(B, n, q, r), n, q), n, q, r)
-            assert (C == want).all(), (mode, l, p)
+    pairs = [(l, int(rng.integers(batch))) for l in range(limbs)]
+    offs = [(l * batch + p) * n for l, p in pairs]
+    A, B, C = _gather(a, offs, n), _gather(b, offs, n), _gather(c, offs, n)
+    if bits == 31:
+        kind = "ref_cyclic" if mode == bc.CYCLIC else "ref_negacyclic"
+    else:
+        kind = "exact_cyclic" if mode == bc.CYCLIC else "exact_negacyclic"
+    want = O.batch_polymul(kind, A, B, n, [qs[l] for l, _ in pairs], [roots[l] for l, _ in pairs])
+    for k, (l, p) in enumerate(pairs):
+        sl = slice(k * n, (k + 1) * n)
+        assert (C[sl] == want[sl]).all(), (bits, mode, l, p)
     plan.close()
