@@ -90,12 +90,15 @@ struct TableGen {
     uint64_t q = 0, ninv = 0;
     std::vector<uint64_t> pw;  // powers of the table's base root
 
+    bool gs_fold = false;  // cyclic inverse: N^-1 on the first entry (a GS network's last stage)
+
     void init(uint32_t logn, int md, bool inv, uint64_t modulus, uint64_t root, uint64_t inv_root,
-              uint64_t n_inverse) {
+              uint64_t n_inverse, bool fold_first = false) {
         L = logn;
         N = 1u << logn;
         mode = md;
         inverse = inv;
+        gs_fold = fold_first;
         q = modulus;
         ninv = n_inverse;
         if (mode == BC_NTT_CYCLIC) {
@@ -115,8 +118,9 @@ struct TableGen {
             const uint32_t s = floor_log2(k);
             const uint32_t m = 1u << s, i = k - m;
             w = pw[static_cast<size_t>(s ? bitrev(i, s) : 0) * (N / (2 * m))];
-            // last CT stage of the inverse (m = N/2) carries N^-1
-            if (inverse && m == N / 2) w = mulmod(w, ninv, q);
+            // last CT stage of the inverse (m = N/2) carries N^-1, or, for
+            // the Gentleman-Sande form of the inverse, its last stage (k = 1)
+            if (inverse && (gs_fold ? k == 1 : m == N / 2)) w = mulmod(w, ninv, q);
         } else {
             w = pw[bitrev(k, L)];
             // last GS stage (m = 1) carries N^-1
@@ -127,6 +131,23 @@ struct TableGen {
 };
 
 }  // namespace
+
+// Whether every limb's root of a cyclic plan is a primitive N-th root of
+// unity whose stored inverse is its exact inverse (and N is invertible):
+// then every radix-2 factorisation of the DFT agrees, and a Gentleman-Sande
+// inverse equals the reference's Cooley-Tukey INTT bit for bit.  For any
+// other root the reference's outputs depend on its exact stage structure
+// (fhe_ntt.wgsl:223-241), which only the plan's own CT tables reproduce.
+bool cyclic_roots_primitive(const bc_plan &p) {
+    if (p.mode != BC_NTT_CYCLIC || p.degree < 2) return false;
+    for (uint32_t l = 0; l < p.n_limbs; ++l) {
+        const uint64_t q = p.moduli[l], w = p.roots[l] % q;
+        if (q < 3 || q % 2 == 0 || p.limbs[l].ninv == 0) return false;
+        if (powmod(w, p.degree, q) != 1 || powmod(w, p.degree / 2, q) != q - 1) return false;
+        if (mulmod(w, p.inv_roots[l] % q, q) != 1) return false;
+    }
+    return true;
+}
 
 int plan_build_host(bc_plan &p, uint32_t degree, uint32_t n_limbs, const uint64_t *moduli,
                     const uint64_t *roots, const uint64_t *inv_roots, int mode,
@@ -346,7 +367,8 @@ enum class PolymulPath { Smem, Fast, Unfused };
 PolymulPath polymul_path(const bc_plan *p, const KArgs &a) {
     const auto aligned = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     const bool all_alias = a.in == a.out && a.in2 == a.out;
-    if (p->mode == BC_NTT_NEGACYCLIC && p->kind == KernelKind::Cluster && fast_layout_ok(a) &&
+    const bool fused_mode = p->mode == BC_NTT_NEGACYCLIC || p->d_tw_gs_fast != nullptr;
+    if (fused_mode && p->kind == KernelKind::Cluster && fast_layout_ok(a) &&
         aligned(a.in2) && !all_alias &&
         fast_variant_for(p->word, p->logn, false) == fast_variant_for(p->word, p->logn, true))
         return PolymulPath::Fast;
@@ -379,9 +401,11 @@ int run_polymul_impl(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t
         a.tw2 = p->d_tw_inv;
         return launch_polymul_smem(p->word, cyclic, a, s);
     case PolymulPath::Fast: {
-        // Negacyclic, fast schedules: C <- NTT(y), then one fused kernel
-        // C <- INTT(NTT(x) * C).  The product commutes, so when A aliases C
-        // the roles swap and A's transform is the one written into C.
+        // Fast schedules: C <- NTT(y), then one fused kernel
+        // C <- INTT(NTT(x) * C), the inverse as a Gentleman-Sande network
+        // (the negacyclic inverse table, or the cyclic plan's GS table).
+        // The product commutes, so when A aliases C the roles swap and A's
+        // transform is the one written into C.
         const uint64_t *x = a_, *y = b;
         if (x == c) std::swap(x, y);
         KArgs f = a;
@@ -392,7 +416,7 @@ int run_polymul_impl(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t
         a.in = x;
         a.in2 = c;
         a.tw = p->d_tw_fwd_fast;
-        a.tw2 = p->d_tw_inv_fast;
+        a.tw2 = cyclic ? p->d_tw_gs_fast : p->d_tw_inv_fast;
         return launch_polymul_fast(p->word, a, s);
     }
     default: break;
@@ -404,17 +428,21 @@ int run_polymul_impl(bc_plan *p, const uint64_t *a_, const uint64_t *b, uint64_t
                     layout->limb_stride == static_cast<int64_t>(batch) * p->degree);
     if (!caller_compact)
         return fail(BC_ERR_UNSUPPORTED, "polymul above the fused size needs the default layout");
+    // The temporary comes from the context's stream-ordered pool and is
+    // released on the same stream after the last launch that reads it, so
+    // the call neither synchronizes nor frees memory another stream uses.
     const size_t words = (static_cast<size_t>(batch) * p->n_limbs) << p->logn;
-    uint64_t *tmp = nullptr;
-    cudaError_t e = cudaMalloc(&tmp, 2 * words * sizeof(uint64_t));
+    void *raw = nullptr;
+    cudaError_t e = cudaMallocFromPoolAsync(&raw, 2 * words * sizeof(uint64_t), p->ctx->pool, s);
     if (e != cudaSuccess) return cuda_fail(e, "polymul scratch allocation");
+    uint64_t *tmp = static_cast<uint64_t *>(raw);
     int r = run_transform(p, false, a_, tmp, batch, layout, s);
     if (!r) r = run_transform(p, false, b, tmp + words, batch, layout, s);
     if (!r) r = run_pointwise(p, tmp, tmp + words, tmp, batch, layout, s);
     if (!r) r = run_transform(p, true, tmp, c, batch, layout, s);
-    cudaStreamSynchronize(s);
-    cudaFree(tmp);
-    return r;
+    e = cudaFreeAsync(raw, s);
+    if (r) return r;
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "polymul scratch release");
 }
 
 }  // namespace
@@ -629,16 +657,39 @@ int bc_plan_create(bc_ctx *ctx, uint32_t degree, uint32_t n_limbs, const uint64_
         return st;
     }
     // the fast kernels read each direction's table in their own layout
-    std::vector<unsigned char> fwd_fast, inv_fast;
+    std::vector<unsigned char> fwd_fast, inv_fast, gs_fast;
     if (p->kind == KernelKind::Cluster) {
         const size_t entry = p->word == Word::W64 ? 16 : 8;
         const int pair = p->word == Word::W64 ? 1 : 2;
         const uint64_t N = degree;
-        for (int t = 0; t < 2; ++t) {
-            const std::vector<unsigned char> &src = t == 0 ? fwd : inv;
-            std::vector<unsigned char> &dst = t == 0 ? fwd_fast : inv_fast;
+        const bool w32 = p->word != Word::W64;
+        const int vf = fast_variant_for(p->word, p->logn, false), vi = fast_variant_for(p->word, p->logn, true);
+        const bool gs = p->mode == BC_NTT_CYCLIC && vf == vi && cyclic_roots_primitive(*p);
+        for (int t = 0; t < (gs ? 3 : 2); ++t) {
+            std::vector<unsigned char> gs_plain;
+            if (t == 2) {  // cyclic inverse in Gentleman-Sande form
+                gs_plain.assign(inv.size(), 0);
+                for (uint32_t l = 0; l < n_limbs; ++l) {
+                    TableGen g;
+                    const uint64_t q = p->moduli[l];
+                    g.init(p->logn, p->mode, true, q, p->roots[l], p->inv_roots[l], p->limbs[l].ninv, true);
+                    unsigned char *base = gs_plain.data() + entry * N * l;
+                    for (uint64_t k = 1; k < N; ++k) {
+                        const uint64_t w = g.value(static_cast<uint32_t>(k));
+                        if (w32) {
+                            uint32_t pr[2] = {static_cast<uint32_t>(w), shoup32(static_cast<uint32_t>(w), static_cast<uint32_t>(q))};
+                            std::memcpy(base + entry * k, pr, 8);
+                        } else {
+                            uint64_t pr[2] = {w, shoup64(w, q)};
+                            std::memcpy(base + entry * k, pr, 16);
+                        }
+                    }
+                }
+            }
+            const std::vector<unsigned char> &src = t == 0 ? fwd : t == 1 ? inv : gs_plain;
+            std::vector<unsigned char> &dst = t == 0 ? fwd_fast : t == 1 ? inv_fast : gs_fast;
             dst.assign(src.size(), 0);
-            const int V = fast_variant_for(p->word, p->logn, t == 1);
+            const int V = t == 0 ? vf : vi;
             std::vector<uint64_t> map(N);
             for (uint64_t k = 1; k < N; ++k) map[k] = fast_table_index(p->logn, V, k, pair);
             for (uint32_t l = 0; l < n_limbs; ++l) {
@@ -647,6 +698,7 @@ int bc_plan_create(bc_ctx *ctx, uint32_t degree, uint32_t n_limbs, const uint64_
                 for (uint64_t k = 1; k < N; ++k) std::memcpy(db + entry * map[k], sb + entry * k, entry);
             }
         }
+        p->table_bytes += gs_fast.size();
     }
     std::vector<CoeffConst> coeff(n_limbs);
     for (uint32_t l = 0; l < n_limbs; ++l) coeff[l] = coeff_const(p->moduli[l]);
@@ -663,6 +715,9 @@ int bc_plan_create(bc_ctx *ctx, uint32_t degree, uint32_t n_limbs, const uint64_
         e = cudaMemcpyAsync(p->d_tw_fwd_fast, fwd_fast.data(), fwd_fast.size(), cudaMemcpyHostToDevice, ctx->stream);
     if (e == cudaSuccess && !inv_fast.empty())
         e = cudaMemcpyAsync(p->d_tw_inv_fast, inv_fast.data(), inv_fast.size(), cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess && !gs_fast.empty()) e = cudaMalloc(&p->d_tw_gs_fast, gs_fast.size());
+    if (e == cudaSuccess && !gs_fast.empty())
+        e = cudaMemcpyAsync(p->d_tw_gs_fast, gs_fast.data(), gs_fast.size(), cudaMemcpyHostToDevice, ctx->stream);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(p->d_limbs, p->limbs.data(), sizeof(LimbConst) * n_limbs,
                             cudaMemcpyHostToDevice, ctx->stream);
@@ -690,6 +745,7 @@ int bc_plan_destroy(bc_plan *p) {
     cudaFree(p->d_tw_inv);
     cudaFree(p->d_tw_fwd_fast);
     cudaFree(p->d_tw_inv_fast);
+    cudaFree(p->d_tw_gs_fast);
     delete p;
     return BC_OK;
 }

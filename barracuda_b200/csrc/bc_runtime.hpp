@@ -51,6 +51,11 @@ struct bc_plan {
     void *d_tw_inv = nullptr;  // inverse table (CT for cyclic, GS for negacyclic), N^-1 folded
     void *d_tw_fwd_fast = nullptr;  // the same tables in the fast kernels' layout
     void *d_tw_inv_fast = nullptr;
+    // Cyclic plans whose roots are all primitive N-th roots with inv_root =
+    // root^-1: the inverse as a Gentleman-Sande network (fast layout, N^-1
+    // folded into its last stage), which exactly undoes the forward and so
+    // lets the fused product serve cyclic plans.  Null otherwise.
+    void *d_tw_gs_fast = nullptr;
     uint64_t table_bytes = 0;
 };
 
@@ -63,6 +68,9 @@ int cuda_fail(cudaError_t e, const char *what);
 // Host-side table entry (w, w') of limb `limb`; table 0 forward, 1 inverse.
 void table_entry(const bc_plan &p, uint32_t limb, int table, uint32_t k, uint64_t *w,
                  uint64_t *wq);
+// Whether a cyclic plan's roots allow the Gentleman-Sande form of its inverse
+// (every root a primitive N-th root, inv_root its exact inverse).
+bool cyclic_roots_primitive(const bc_plan &p);
 // Builds limb constants and tables on the host (no device work).
 int plan_build_host(bc_plan &p, uint32_t degree, uint32_t n_limbs, const uint64_t *moduli,
                     const uint64_t *roots, const uint64_t *inv_roots, int mode,

@@ -1,24 +1,23 @@
 // bc_static_scratch.cu -- bc_polymul_static_scratch: the NTT-based
 // polynomial product without any device allocation.
 //
-// On its unfused path (cyclic plans above the fused size, layouts the fused
-// kernels cannot take) bc_polymul runs forward(A) and forward(B) into a
-// temporary device buffer, multiplies, and runs the inverse; it allocates
-// that buffer with cudaMalloc, synchronizes the stream and frees it on every
-// call.  Some callers cannot do that during the call:
+// On its unfused path (N >= 2^18, cyclic plans with a non-primitive root
+// above the fused size, layouts the fused kernels cannot take) bc_polymul
+// runs forward(A) and forward(B) into a temporary, multiplies, and runs the
+// inverse; it takes that temporary from the context's stream-ordered memory
+// pool on every call, which grows the pool with fresh device memory when it
+// holds none free.  Some callers cannot allocate during the call:
 //   - processes whose device memory was reserved up front by another
 //     allocator (a framework's caching pool holding the free memory), where
-//     cudaMalloc has nothing left to hand out;
-//   - serving loops that keep work in flight on several streams, where the
-//     implicit device-wide synchronization of cudaFree stalls every other
-//     stream.
+//     the driver has nothing left to hand out;
+//   - serving loops under a fixed device-memory budget that must not grow
+//     once they run.
 // This entry point keeps the temporary in one fixed buffer per device in the
 // library's static device memory instead, so it allocates nothing and does
 // not synchronize.  The price is a size limit and a shared buffer: calls that
 // overlap in time on one GPU race on it (see barracuda_fhe.h).
 #include <cstdint>
 #include <cstring>
-#include <mutex>
 
 #include <cuda_runtime.h>
 
@@ -39,25 +38,21 @@ constexpr int kMaxDevices = 64;
 // written before it is read, so nothing here needs to start at zero.
 static __device__ __align__(256) uint64_t g_polymul_scratch[2 * kMaxCoeffs];
 
-std::mutex g_addr_mu;
-uint64_t *g_addr[kMaxDevices] = {};
-
-// Device address of the static buffer on the current device (`device`),
-// looked up once per device.  The lookup may make the driver load this
-// translation unit's device module; that is the set-up the first call does.
+// Device address of the static buffer on the current device (`device`).
+// Looked up on every call rather than cached: after a device reset the
+// driver reloads the module and the buffer may move, and the lookup is cheap
+// once the module is loaded.  The first lookup on a device may make the
+// driver load this translation unit's device module; that is the set-up the
+// first call does.
 int scratch_address(int device, uint64_t **out) {
     if (device < 0 || device >= kMaxDevices)
         return fail(BC_ERR_UNSUPPORTED,
                     format("bc_polymul_static_scratch supports device ordinals below %d, got %d",
                            kMaxDevices, device));
-    std::lock_guard<std::mutex> lk(g_addr_mu);
-    if (!g_addr[device]) {
-        void *ptr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_polymul_scratch);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(polymul static scratch)");
-        g_addr[device] = static_cast<uint64_t *>(ptr);
-    }
-    *out = g_addr[device];
+    void *ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_polymul_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(polymul static scratch)");
+    *out = static_cast<uint64_t *>(ptr);
     return BC_OK;
 }
 

@@ -269,16 +269,20 @@ int bc_ntt_inverse_mul(bc_plan *plan, const uint64_t *d_a_hat, const uint64_t *d
 /* C = A * B mod q_l, coefficient-wise. */
 int bc_pointwise_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                      uint32_t batch, const bc_layout *layout, void *stream);
-/* C = INTT(NTT(A) * NTT(B)) per (limb, polynomial).  Negacyclic plans on
- * the cluster kernels (N >= 2^10, 16-byte aligned operands, even strides, not
- * A == B == C) run two launches: NTT(B) into C, then one fused kernel
- * C = INTT(NTT(A) * C).  Otherwise, up to N = 2^14 (moduli below 2^31) or
- * 2^13 (wider moduli), one fused shared-memory kernel.  Neither allocates.
- * Every other case (cyclic plans above the fused size, other layouts)
- * transforms both operands into a temporary device buffer, multiplies and
- * runs the inverse into C, needing the default layout (layout NULL or
- * compact); that temporary is allocated, the stream synchronized and the
- * buffer freed on every call. */
+/* C = INTT(NTT(A) * NTT(B)) per (limb, polynomial).  On the cluster kernels
+ * (2^10 <= N <= 2^17, 16-byte aligned operands, even strides, not
+ * A == B == C) negacyclic plans, and cyclic plans whose roots are all
+ * primitive N-th roots of unity with inv_root = root^-1, run two launches:
+ * NTT(B) into C, then one fused kernel C = INTT(NTT(A) * C) whose inverse is
+ * a Gentleman-Sande network (for those roots it equals the reference's
+ * FheFastPolyMul chain bit for bit).  Otherwise, up to N = 2^14 (moduli below
+ * 2^31) or 2^13 (wider moduli), one fused shared-memory kernel.  Neither
+ * allocates.  Every other case (N >= 2^18, cyclic plans with a non-primitive
+ * root above the fused size, other layouts) transforms both operands into a
+ * temporary, multiplies and runs the inverse into C, needing the default
+ * layout (layout NULL or compact); the temporary comes from the context's
+ * stream-ordered memory pool and is released on the same stream, so the call
+ * does not synchronize. */
 int bc_polymul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                uint32_t batch, const bc_layout *layout, void *stream);
 
@@ -291,15 +295,15 @@ int bc_polymul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t
  * reference: FheFastPolyMul::execute (ops/fhe_fast_poly_mul.rs:122)
  * allocates its intermediates and output on every call.
  *
- * Who needs it: on its unfused path (see bc_polymul: cyclic plans above
- * N = 2^14 for moduli below 2^31 or 2^13 otherwise, layouts the fused
- * kernels cannot take) bc_polymul allocates a temporary device buffer,
- * synchronizes the stream and frees the buffer on every call.  A caller
- * cannot afford that when the device memory is already reserved by another
- * allocator (a framework's caching pool leaves cudaMalloc nothing to hand
- * out), or when it keeps work in flight on several streams and cudaFree's
- * implicit device-wide synchronization would stall them.  This entry point
- * keeps the temporary in one fixed buffer per device in the library's static
+ * Who needs it: on its unfused path (see bc_polymul: N >= 2^18, cyclic plans
+ * with a non-primitive root above the fused size, layouts the fused kernels
+ * cannot take) bc_polymul takes a temporary from the context's memory pool
+ * on every call, and the pool grows with fresh device memory when it holds
+ * none free.  A caller cannot afford that when the device memory is already
+ * reserved by another allocator (a framework's caching pool leaves the
+ * driver nothing to hand out), or when it runs under a fixed device-memory
+ * budget that steady-state serving must not grow.  This entry point keeps
+ * the temporary in one fixed buffer per device in the library's static
  * device memory instead.  It computes the same result as bc_polymul and
  * neither allocates nor synchronizes.
  *
@@ -314,10 +318,12 @@ int bc_polymul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t
  * give wrong results: other streams, other host threads, other plans or
  * contexts on the same GPU.  The caller must serialize them.
  *
- * Set-up: the first call on each device looks up the buffer's device
- * address, which may make the driver load the library's device code.  Make
- * that first call before any stream capture.  Nothing in the buffer needs
- * to start at zero: every word is written before it is read. */
+ * Set-up: every call looks up the buffer's device address on the current
+ * device (cudaGetSymbolAddress), so the address stays right after a device
+ * reset; the first call on each device may make the driver load the
+ * library's device code, so make that first call before any stream capture.
+ * Nothing in the buffer needs to start at zero: every word is written
+ * before it is read. */
 int bc_polymul_static_scratch(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b,
                               uint64_t *d_c, uint32_t batch, const bc_layout *layout,
                               void *stream);

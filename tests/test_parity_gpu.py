@@ -548,11 +548,39 @@ def test_plan_pointwise(device):
         assert (C[sl] == O.ref_pointwise(A[sl], B[sl], batch * n, qs[l])).all()
 
 
+@pytest.mark.parametrize("logn", [15, 18])
+def test_cyclic_polymul_non_primitive_root_takes_the_reference_chain(device, logn):
+    """A cyclic root that is not a primitive N-th root (here an N/2-th root)
+    keeps the reference's stage structure: bc_polymul takes the unfused chain
+    through a pool temporary and equals FheFastPolyMul's output bit for bit.
+    N = 2^18 is above the cluster kernels, where every cyclic product takes
+    that chain."""
+    n, limbs, batch = 1 << logn, 2, 2
+    qs = bc.ntt_primes(31, n, limbs)
+    psis = [bc.negacyclic_root(q, n) for q in qs]
+    roots = [pow(p, 4, q) for p, q in zip(psis, qs)] if logn == 15 else [p * p % q for p, q in zip(psis, qs)]
+    plan = bc.NttPlan(device, n, qs, roots, mode=bc.CYCLIC)
+    total = limbs * batch * n
+    a, b, c = _alloc(device, total), _alloc(device, total), _alloc(device, total)
+    plan.fill_uniform(a, batch, seed=5)
+    plan.fill_uniform(b, batch, seed=6)
+    for _ in range(2):  # the pool temporary is reused by the second call
+        plan.polymul(a, b, c, batch)
+    device.synchronize()
+    A, B, C = a.to_u64(), b.to_u64(), c.to_u64()
+    for l in range(limbs):
+        off = (l * batch + 1) * n
+        want = O.ref_fast_poly_mul(A[off:off + n], B[off:off + n], n, qs[l], roots[l])
+        assert (C[off:off + n] == want).all(), (logn, l)
+    plan.close()
+
+
+@pytest.mark.parametrize("mode", [bc.NEGACYCLIC, bc.CYCLIC])
 @pytest.mark.parametrize("bits", [31, 60])
-def test_polymul_aliasing(device, bits):
+def test_polymul_aliasing(device, bits, mode):
     """C may alias A, B or both (squaring in place); results as with separate buffers."""
     n, limbs, batch = 1 << 15, 2, 2
-    plan, qs, roots = _plan(device, n, limbs, bits, bc.NEGACYCLIC)
+    plan, qs, roots = _plan(device, n, limbs, bits, mode)
     total = limbs * batch * n
     a, b, c, ref, sq = (_alloc(device, total) for _ in range(5))
     plan.fill_uniform(a, batch, seed=3)
