@@ -92,7 +92,26 @@ def build(clean: bool = False, jobs: int | None = None, verbose: bool = False,
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}{r.stdout}")
+    build_probe()
     return LIB
+
+
+PROBE_SRC = os.path.join(PKG, "probe", "op_latency.cpp")
+PROBE = os.path.join(LIBDIR, "bc_op_latency")
+
+
+def build_probe() -> str:
+    """The C-ABI latency probe run by bench.py --op-latency (host code only)."""
+    if _stale(PROBE, [PROBE_SRC, LIB, os.path.join(INCLUDE, "barracuda_fhe.h")]):
+        cxx = shutil.which("g++") or shutil.which("c++")
+        if not cxx:
+            raise RuntimeError("g++ not found for the latency probe")
+        cmd = [cxx, "-O2", "-std=c++17", "-I", INCLUDE, "-o", PROBE, PROBE_SRC, "-L", LIBDIR,
+               "-lbarracuda_fhe", "-Wl,-rpath,$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"latency probe build failed:\n{r.stderr}{r.stdout}")
+    return PROBE
 
 
 def main(argv=None):

@@ -9,10 +9,20 @@
 
 namespace bc {
 
-// Bits OR-ed into the context's device status word by kernels.
+// Flags kernels write into the context's status word.  The word lives in
+// mapped, page-locked host memory: a kernel that finds a bad input stores its
+// flag with a plain store (no device atomics to host memory), and the host
+// reads the word after waiting for the stream, with no copy.  Each kernel
+// only ever stores the same flag value, so plain stores cannot lose a flag.
 enum : uint32_t {
     kStatusInputRange = 1u,  // a coefficient >= 2^32 reached a 32-bit-word plan
 };
+
+#ifdef __CUDACC__
+__device__ __forceinline__ void store_status(uint32_t *status, uint32_t flag) {
+    *reinterpret_cast<volatile uint32_t *>(status) = flag;
+}
+#endif
 
 // Maps a CUDA error to a status and records the message (bc_runtime.cpp).
 int cuda_fail(cudaError_t e, const char *what);

@@ -26,7 +26,7 @@ __device__ __forceinline__ uint32_t brev_bits(uint32_t x, uint32_t bits) {
 
 __device__ __forceinline__ void raise_status(uint32_t *status, bool bad, uint32_t bit) {
     if (__any_sync(0xffffffffu, bad)) {
-        if ((threadIdx.x & 31) == 0) atomicOr(status, bit);
+        if ((threadIdx.x & 31) == 0) store_status(status, bit);
     }
 }
 

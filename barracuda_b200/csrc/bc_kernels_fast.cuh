@@ -655,7 +655,7 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, PF>
         const typename A::Tw *tw = reinterpret_cast<const typename A::Tw *>(a.tw) + (static_cast<size_t>(limb) << L);
         In::load(work, a.in + base_of(cl), rank, lc, bad);
         if constexpr (A::kBits == 32) {
-            if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) atomicOr(a.status, kStatusInputRange);
+            if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) store_status(a.status, kStatusInputRange);
         }
         typename First::Ring ring;
         First::prefetch(ring, tw, rank);
@@ -680,7 +680,7 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, PF>
         __syncthreads();
     }
     if constexpr (A::kBits == 32) {
-        if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) atomicOr(a.status, kStatusInputRange);
+        if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) store_status(a.status, kStatusInputRange);
     }
 }
 
@@ -778,7 +778,7 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, fal
     Inv::run(work, tw2, lc, rank, ring_i);
     Out::store(work, a.out + base, rank, lc);
     if constexpr (A::kBits == 32) {
-        if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) atomicOr(a.status, kStatusInputRange);
+        if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) store_status(a.status, kStatusInputRange);
     }
 }
 
@@ -824,7 +824,7 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, fal
     if constexpr (!INV) Out::mul(work, a.in2 + base, rank, lc, bad);
     Out::store(work, a.out + base, rank, lc);
     if constexpr (A::kBits == 32) {
-        if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) atomicOr(a.status, kStatusInputRange);
+        if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) store_status(a.status, kStatusInputRange);
     }
 }
 

@@ -3,6 +3,7 @@
 #include "bc_runtime.hpp"
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <thread>
 
@@ -33,14 +34,28 @@ int use_device(const bc_ctx *ctx) {
     return e == cudaSuccess ? BC_OK : cuda_fail(e, "cudaSetDevice");
 }
 
+// Waits for `s`: polls for a short while first (a single reference-op call
+// finishes within microseconds, and a blocking wait adds the thread's wake-up
+// latency on top), then blocks.
+cudaError_t wait_stream(cudaStream_t s) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(s);
+        if (q != cudaErrorNotReady) return q;
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::microseconds(200)) break;
+    }
+    return cudaStreamSynchronize(s);
+}
+
 int ctx_sync(bc_ctx *ctx) {
-    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    // kernels store into the mapped status word; once the stream is done its
+    // value is visible on the host without a copy
+    const cudaError_t e = wait_stream(ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
-    uint32_t st = 0;
-    e = cudaMemcpy(&st, ctx->d_status, sizeof st, cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) return cuda_fail(e, "status readback");
+    volatile uint32_t *hs = ctx->h_status;
+    const uint32_t st = *hs;
     if (st) {
-        cudaMemset(ctx->d_status, 0, sizeof st);
+        *hs = 0;
         if (st & kStatusInputRange)
             return fail(BC_ERR_INVALID_INPUT,
                         "coefficient >= 2^32 given to a transform whose moduli are below 2^31 "
@@ -521,18 +536,24 @@ int bc_ctx_create(int device, bc_ctx **out) {
         delete c;
         return cuda_fail(e, "cudaStreamCreate");
     }
-    if ((e = cudaMalloc(&c->d_status, sizeof(uint32_t))) != cudaSuccess ||
-        (e = cudaMemset(c->d_status, 0, sizeof(uint32_t))) != cudaSuccess) {
+    // status word: mapped page-locked host memory (see bc_kernels.hpp)
+    void *hs = nullptr, *ds = nullptr;
+    if ((e = cudaHostAlloc(&hs, sizeof(uint32_t), cudaHostAllocMapped | cudaHostAllocPortable)) != cudaSuccess ||
+        (e = cudaHostGetDevicePointer(&ds, hs, 0)) != cudaSuccess) {
+        if (hs) cudaFreeHost(hs);
         cudaStreamDestroy(c->stream);
         delete c;
         return cuda_fail(e, "status word allocation");
     }
+    c->h_status = static_cast<uint32_t *>(hs);
+    c->d_status = static_cast<uint32_t *>(ds);
+    *c->h_status = 0;
     cudaMemPoolProps props = {};
     props.allocType = cudaMemAllocationTypePinned;
     props.location.type = cudaMemLocationTypeDevice;
     props.location.id = device;
     if ((e = cudaMemPoolCreate(&c->pool, &props)) != cudaSuccess) {
-        cudaFree(c->d_status);
+        cudaFreeHost(c->h_status);
         cudaStreamDestroy(c->stream);
         delete c;
         return cuda_fail(e, "memory pool creation");
@@ -550,7 +571,7 @@ int bc_ctx_destroy(bc_ctx *ctx) {
     use_device(ctx);
     cudaStreamSynchronize(ctx->stream);
     ctx->cache.clear();  // destroys the cached plans (no caller holds one now)
-    cudaFree(ctx->d_status);
+    cudaFreeHost(ctx->h_status);  // d_status is its device mapping
     cudaStreamDestroy(ctx->stream);
     // returns at once; the pool goes once its last stream-ordered free completes
     if (ctx->pool) cudaMemPoolDestroy(ctx->pool);
@@ -576,21 +597,30 @@ int bc_ctx_sync(bc_ctx *ctx) {
     return st ? st : ctx_sync(ctx);
 }
 
+// Buffers come from the context's memory pool, which keeps freed memory for
+// reuse: a reference-op call that allocates its output (FheNtt::execute
+// returns a new tensor) then costs no driver allocation.  The guarantees of
+// cudaMalloc / cudaFree stay: the memory is usable by every stream when
+// bc_buf_alloc returns (the context stream is idle, or is waited for), and
+// bc_buf_free first waits for all work on the device, as cudaFree does.
 int bc_buf_alloc(bc_ctx *ctx, size_t bytes, void **dptr) {
     if (!ctx || !dptr) return fail(BC_ERR_INVALID_INPUT, "NULL argument");
     *dptr = nullptr;
     int st = use_device(ctx);
     if (st) return st;
-    const cudaError_t e = cudaMalloc(dptr, bytes ? bytes : 1);
-    return e == cudaSuccess ? BC_OK : cuda_fail(e, "cudaMalloc");
+    cudaError_t e = cudaMallocFromPoolAsync(dptr, bytes ? bytes : 1, ctx->pool, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "device buffer allocation");
+    if (cudaStreamQuery(ctx->stream) != cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "device buffer allocation");
 }
 
 int bc_buf_free(bc_ctx *ctx, void *dptr) {
     if (!ctx) return fail(BC_ERR_INVALID_INPUT, "NULL context");
     if (!dptr) return BC_OK;
     use_device(ctx);
-    const cudaError_t e = cudaFree(dptr);
-    return e == cudaSuccess ? BC_OK : cuda_fail(e, "cudaFree");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaFreeAsync(dptr, ctx->stream);
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "device buffer release");
 }
 
 static int copy_sync(bc_ctx *ctx, void *dst, const void *src, size_t bytes, cudaMemcpyKind k) {

@@ -19,7 +19,8 @@ struct bc_plan;
 struct bc_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
-    uint32_t *d_status = nullptr;
+    uint32_t *h_status = nullptr;  // status word: mapped page-locked host memory
+    uint32_t *d_status = nullptr;  // its device address (what kernels store to)
     // Stream-ordered pool for per-call temporaries (multi-pass transforms):
     // each call allocates and frees on its own stream, so calls on several
     // streams never share or free a buffer another stream still uses.

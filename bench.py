@@ -560,6 +560,7 @@ def _run_sweep(args, torch, bc, group, world, rank, local):
 # transform.  name -> (log2 N, limbs, kernel name, algorithmic bytes per word)
 KERNEL_CASES = {
     "polymul": (15, 32, "k_polymul_fast", 40),       # NTT(B) into C, then the fused kernel
+    "polymul_cyclic": (15, 32, "k_polymul_fast", 40),  # the same for a cyclic plan (primitive roots)
     "automorphism_smem": (13, 16, "k_automorph_smem", 16),
     "automorphism_cluster": (14, 16, "k_automorph_cluster", 16),
     "automorphism_gather": (16, 16, "k_automorph_gather", 16),
@@ -594,7 +595,11 @@ def run_kernel_case(args):
     words = 1 << 25
     batch = words // (n * limbs)
     qs = bc.ntt_primes(31, n, limbs)
-    plan = bc.NttPlan(dev, n, qs, [bc.negacyclic_root(q, n) for q in qs], mode=bc.NEGACYCLIC)
+    psis = [bc.negacyclic_root(q, n) for q in qs]
+    if case.endswith("_cyclic"):
+        plan = bc.NttPlan(dev, n, qs, [p * p % q for p, q in zip(psis, qs)], mode=bc.CYCLIC)
+    else:
+        plan = bc.NttPlan(dev, n, qs, psis, mode=bc.NEGACYCLIC)
     a = torch.empty(words, dtype=torch.int64, device="cuda")
     b = torch.empty_like(a)
     c = torch.empty(words * (3 if case == "decompose" else 1), dtype=torch.int64, device="cuda")
@@ -602,6 +607,7 @@ def run_kernel_case(args):
     plan.fill_uniform(b, batch, seed=2, stream=sh)
     ops = {
         "polymul": lambda: plan.polymul(a, b, c, batch, stream=sh),
+        "polymul_cyclic": lambda: plan.polymul(a, b, c, batch, stream=sh),
         "automorphism_smem": lambda: plan.automorphism(a, c, batch, 2469, stream=sh),
         "automorphism_cluster": lambda: plan.automorphism(a, c, batch, 2469, stream=sh),
         "automorphism_gather": lambda: plan.automorphism(a, c, batch, 2469, stream=sh),
@@ -635,6 +641,80 @@ def run_kernel_case(args):
     dev.close()
 
 
+def run_op_latency(args):
+    """Single synchronous calls of the reference op API at N = 4096 (q < 2^31),
+    median over `--steps` calls after `--warmup`: (1) through the public op
+    mirror (FheNtt.new(...).execute() and friends: output allocation, launch,
+    wait), (2) through the C ABI into a preallocated output (launch and wait
+    only).  One JSON line, microseconds per call."""
+    import time
+
+    import numpy as np
+
+    import barracuda_b200 as bc
+    from barracuda_b200 import _native as NN
+
+    dev = bc.Device(0)
+    n = 4096
+    q = bc.ntt_prime(31, n, 0)
+    w = pow(bc.negacyclic_root(q, n), 2, q)
+    winv = pow(w, -1, q)
+    rng = np.random.default_rng(1)
+    a = bc.create_fhe_poly_tensor(rng.integers(0, q, n, dtype=np.uint64), dev)
+    b = bc.create_fhe_poly_tensor(rng.integers(0, q, n, dtype=np.uint64), dev)
+    out = bc.FheTensor(dev, 2 * n)
+    lib = NN.lib()
+    api = {
+        "FheNtt": lambda: bc.FheNtt.new(a, n, q, w).execute(),
+        "FheIntt": lambda: bc.FheIntt.new(a, n, q, winv).execute(),
+        "FhePointwiseMul": lambda: bc.FhePointwiseMul.new(a, b, n, q).execute(),
+        "FheFastPolyMul": lambda: bc.FheFastPolyMul.new(a, b, n, q, w).execute(),
+    }
+    cabi = {
+        "FheNtt": lambda: lib.bc_fhe_ntt(dev.handle, a.ptr, 2 * n, n, q, w, out.ptr),
+        "FheIntt": lambda: lib.bc_fhe_intt(dev.handle, a.ptr, 2 * n, n, q, winv, out.ptr),
+        "FhePointwiseMul": lambda: lib.bc_fhe_pointwise_mul(dev.handle, a.ptr, 2 * n, b.ptr, 2 * n, n, q, out.ptr),
+        "FheFastPolyMul": lambda: lib.bc_fhe_fast_poly_mul(dev.handle, a.ptr, 2 * n, b.ptr, 2 * n, n, q, w, out.ptr),
+    }
+    plan = bc.NttPlan(dev, n, [q], [w], mode=bc.CYCLIC)
+    parts = {
+        "ctx_sync_idle": lambda: lib.bc_ctx_sync(dev.handle),
+        "plan_forward_and_sync": lambda: (lib.bc_ntt_forward(plan.handle, a.ptr, out.ptr, 1, None, None),
+                                          lib.bc_ctx_sync(dev.handle))[1],
+    }
+    res = {"op_api_us": {}, "c_abi_us": {}, "parts_us": {}}
+    steps = max(args.steps, 50)
+    for key, table in (("op_api_us", api), ("c_abi_us", cabi), ("parts_us", parts)):
+        for name, fn in table.items():
+            for _ in range(max(args.warmup, 5)):
+                r = fn()
+                if key == "op_api_us":
+                    r.free()
+            ts = []
+            for _ in range(steps):
+                t0 = time.perf_counter()
+                r = fn()
+                ts.append((time.perf_counter() - t0) * 1e6)
+                if key == "op_api_us":
+                    r.free()
+                else:
+                    NN.check(r)
+            res[key][name] = round(statistics.median(ts), 2)
+    # the same calls from C (what a Rust or C caller sees, without Python's ctypes)
+    probe = os.path.join(ROOT, "barracuda_b200", "lib", "bc_op_latency")
+    c_level = None
+    if os.path.exists(probe):
+        r = subprocess.run([probe, str(max(steps, 200))], capture_output=True, text=True)
+        if r.returncode == 0 and r.stdout.strip():
+            c_level = json.loads(r.stdout.strip().splitlines()[-1])
+    print(json.dumps({"op_latency": True, "N": n, "q_bits": 31, "calls": steps,
+                      "timing": "host wall clock per synchronous call (perf_counter), median", **res,
+                      "from_c": c_level}),
+          flush=True)
+    plan.close()
+    dev.close()
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -651,6 +731,8 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="per-N forward/inverse report (config 4 shape) instead of the bench line")
+    ap.add_argument("--op-latency", action="store_true",
+                    help="single-call latency of the reference op API at N=4096 (not a bench line)")
     ap.add_argument("--kernel-case", choices=sorted(KERNEL_CASES),
                     help="time one kernel family on a small case (for ncu captures)")
     args = ap.parse_args(argv)
@@ -658,6 +740,8 @@ def main(argv=None):
         args.warmup = 3
     if args.kernel_case:
         run_kernel_case(args)
+    elif args.op_latency:
+        run_op_latency(args)
     elif args.sweep:
         run_sweep(args)
     elif args.impl == "reference":

@@ -89,7 +89,11 @@ int bc_ctx_sync(bc_ctx *ctx);
 
 /* --------------------------------------------------------------- buffers */
 
-/* Device memory owned by the caller; synchronous copies use the ctx stream. */
+/* Device memory owned by the caller; synchronous copies use the ctx stream.
+ * bc_buf_alloc takes the memory from the context's pool (freed buffers are
+ * reused without a driver allocation) and returns it ready for every
+ * stream; bc_buf_free waits for all work on the device, as cudaFree does,
+ * then returns the memory to the pool. */
 int bc_buf_alloc(bc_ctx *ctx, size_t bytes, void **dptr);
 int bc_buf_free(bc_ctx *ctx, void *dptr);
 int bc_buf_h2d(bc_ctx *ctx, void *dst, const void *src, size_t bytes);
