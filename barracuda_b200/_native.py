@@ -127,6 +127,10 @@ SIGNATURES = {
     "bc_pointwise_mul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_ntt_forward_mul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_ntt_inverse_mul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
+    "bc_ntt_forward_add": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
+    "bc_ntt_forward_sub": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
+    "bc_ntt_inverse_add": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
+    "bc_ntt_inverse_sub": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_polymul": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_polymul_static_scratch": (_i32, [_vp, _vp, _vp, _vp, _u32, _lay, _vp]),
     "bc_automorphism": (_i32, [_vp, _vp, _vp, _u32, _lay, _u32, _vp]),

@@ -30,6 +30,10 @@ int cuda_fail(cudaError_t e, const char *what);
 // Arithmetic flavour of a plan (see bc_arith.cuh).
 enum class Word : int { W32Lazy4 = 0, W32Lazy2 = 1, W64 = 2 };
 
+// Pointwise step of the fused transforms (k_ntt_mul_fast): C = NTT(A) op B^
+// or C = INTT(A^ op B^), exact mod q.
+enum FuseOp : uint32_t { kFuseMul = 0, kFuseAdd = 1, kFuseSub = 2 };
+
 // Arguments common to the transform kernels.  Strides are in u64 elements.
 struct KArgs {
     const uint64_t *in;
@@ -40,7 +44,7 @@ struct KArgs {
     uint32_t batch;
     uint32_t n_limbs;
     uint32_t logn;
-    uint32_t pad0;
+    uint32_t op;          // pointwise step of the fused transforms (FuseOp)
     const void *tw;      // table used by the (first) transform, N entries per limb
     const void *tw2;     // table of the second transform (polymul inverse)
     const LimbConst *limbs;
@@ -104,12 +108,15 @@ struct CoeffConst {
     uint32_t pad;
 };
 CoeffConst coeff_const(uint64_t q);  // q != 0
-enum CoeffOp : int { kCoeffAdd = 0, kCoeffSub = 1, kCoeffMul = 2 };
+// Add and Sub follow the reference shaders (exact for inputs below q); the
+// Exact forms reduce both inputs first and are exact for any u64 (the
+// two-launch path of the fused transform-and-add/sub).
+enum CoeffOp : int { kCoeffAdd = 0, kCoeffSub = 1, kCoeffMul = 2, kCoeffAddExact = 3, kCoeffSubExact = 4 };
 // C = A op B for a.batch polynomials of n coefficients per limb (layout
 // strides in `a`); `consts` holds one CoeffConst per limb on the device, or
 // is NULL and `single` serves every limb.
 int launch_coeff_op(int op, const KArgs &a, uint64_t n, const CoeffConst *consts,
-                    const CoeffConst &single, cudaStream_t s);
+                    const CoeffConst &single, cudaStream_t s, bool flag_wide_words = false);
 
 int launch_fill_uniform(const KArgs &a, uint64_t seed, uint64_t first_poly,
                         uint64_t total_polys, cudaStream_t s);

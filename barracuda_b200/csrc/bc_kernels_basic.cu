@@ -321,8 +321,11 @@ __device__ __forceinline__ uint64_t mulmod_any(uint64_t a, uint64_t b, const Coe
     return static_cast<uint64_t>(p % c.q);
 }
 
+// kCoeffAddExact / kCoeffSubExact: (x mod q +- y mod q) mod q for any u64;
+// with `flag_wide`, a word >= 2^32 raises kStatusInputRange as the 32-bit
+// transforms do for their inputs.
 template <int OP>
-__global__ void k_coeff(KArgs a, uint64_t n, const CoeffConst *consts, CoeffConst single) {
+__global__ void k_coeff(KArgs a, uint64_t n, const CoeffConst *consts, CoeffConst single, int flag_wide) {
     const uint64_t polys = static_cast<uint64_t>(a.batch) * a.n_limbs;
     for (uint64_t pl = blockIdx.y; pl < polys; pl += gridDim.y) {
         const uint64_t limb = pl / a.batch, poly = pl % a.batch;
@@ -332,7 +335,16 @@ __global__ void k_coeff(KArgs a, uint64_t n, const CoeffConst *consts, CoeffCons
              j += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
             const uint64_t x = __ldcs(a.in + base + j), y = __ldcs(a.in2 + base + j);
             uint64_t r;
-            if constexpr (OP == kCoeffAdd) {
+            if constexpr (OP == kCoeffAddExact || OP == kCoeffSubExact) {
+                if (flag_wide && ((x | y) >> 32) != 0) store_status(a.status, kStatusInputRange);
+                const uint64_t xr = reduce_any(x, c), yr = reduce_any(y, c);
+                if constexpr (OP == kCoeffAddExact) {
+                    r = xr + yr;  // q < 2^62: no overflow
+                    if (r >= c.q) r -= c.q;
+                } else {
+                    r = xr >= yr ? xr - yr : xr + (c.q - yr);
+                }
+            } else if constexpr (OP == kCoeffAdd) {
                 r = x + y;
                 if (r >= c.q) r -= c.q;
                 if (r >= c.q) r -= c.q;
@@ -539,7 +551,7 @@ CoeffConst coeff_const(uint64_t q) {
 }
 
 int launch_coeff_op(int op, const KArgs &a, uint64_t n, const CoeffConst *consts,
-                    const CoeffConst &single, cudaStream_t s) {
+                    const CoeffConst &single, cudaStream_t s, bool flag_wide_words) {
     const uint64_t polys = static_cast<uint64_t>(a.batch) * a.n_limbs;
     if (n == 0 || polys == 0) return BC_OK;
     const unsigned T = 256;
@@ -547,9 +559,11 @@ int launch_coeff_op(int op, const KArgs &a, uint64_t n, const CoeffConst *consts
     if (bx > 64) bx = 64;
     const dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(polys < 65535 ? polys : 65535));
     switch (op) {
-    case kCoeffAdd: k_coeff<kCoeffAdd><<<grid, T, 0, s>>>(a, n, consts, single); break;
-    case kCoeffSub: k_coeff<kCoeffSub><<<grid, T, 0, s>>>(a, n, consts, single); break;
-    case kCoeffMul: k_coeff<kCoeffMul><<<grid, T, 0, s>>>(a, n, consts, single); break;
+    case kCoeffAdd: k_coeff<kCoeffAdd><<<grid, T, 0, s>>>(a, n, consts, single, 0); break;
+    case kCoeffSub: k_coeff<kCoeffSub><<<grid, T, 0, s>>>(a, n, consts, single, 0); break;
+    case kCoeffMul: k_coeff<kCoeffMul><<<grid, T, 0, s>>>(a, n, consts, single, 0); break;
+    case kCoeffAddExact: k_coeff<kCoeffAddExact><<<grid, T, 0, s>>>(a, n, consts, single, flag_wide_words); break;
+    case kCoeffSubExact: k_coeff<kCoeffSubExact><<<grid, T, 0, s>>>(a, n, consts, single, flag_wide_words); break;
     default: return fail(BC_ERR_INTERNAL, "unknown coefficient op");
     }
     return check_launch("k_coeff");

@@ -468,16 +468,19 @@ struct Coop {
         }
     }
 
-    // Multiplies the CTA's share of the working array, coefficient-wise mod
-    // q, by `src` (in this stage's order): the pointwise product of a fused
-    // polynomial multiplication or transform-and-multiply.  `src` words are
-    // reduced first (any u64 for 64-bit words; words >= 2^32 set `bad` for
-    // 32-bit words, as the input loads do).  Kept out of line: inlined next
-    // to a transform under the 64-register budget, it made the kernels
-    // spill 460-550 bytes per thread inside the passes (ptxas -v); as a call
-    // they spill at most 12.
-    __device__ __noinline__ static void mul(W *smem, const uint64_t *src, uint32_t rank,
-                                            const LimbConst &lc, uint32_t &bad) {
+    // Combines the CTA's share of the working array, coefficient-wise mod q,
+    // with `src` (in this stage's order): OP kFuseMul multiplies (the
+    // pointwise product of a fused polynomial multiplication or
+    // transform-and-multiply), kFuseAdd / kFuseSub add or subtract.  `src`
+    // words are reduced first (any u64 for 64-bit words; words >= 2^32 set
+    // `bad` for 32-bit words, as the input loads do); results stay in the
+    // working array's lazy range.  Kept out of line: inlined next to a
+    // transform under the 64-register budget, it made the kernels spill
+    // 460-550 bytes per thread inside the passes (ptxas -v); as a call they
+    // spill at most 12.
+    template <uint32_t OP>
+    __device__ __noinline__ static void combine(W *smem, const uint64_t *src, uint32_t rank,
+                                                const LimbConst &lc, uint32_t &bad) {
         const uint32_t tid = threadIdx.x;
         const uint32_t kr = NAT ? rank_pos<S>(rank, PHASE) : (__brev(rank_pos<S>(rank, PHASE)) >> (32 - L));
         const uint32_t kt = natural_of<S, L>(2 * tid, PHASE, NAT) + kr;
@@ -496,10 +499,33 @@ struct Coop {
             for (int j = 0; j < kBatch && j0 + j < kIters; ++j) {
                 const uint32_t a0 = at + smem_of_natural<S, L>(natural_of<S, L>(2 * (j0 + j) * T, PHASE, NAT),
                                                                PHASE, NAT);
-                smem[a0] = mulmod_lc(smem[a0], A::load_reduce(x[j].x, q, one_q, bad), lc);
-                smem[a0 + a1] = mulmod_lc(smem[a0 + a1], A::load_reduce(x[j].y, q, one_q, bad), lc);
+                smem[a0] = fuse<OP>(smem[a0], A::load_reduce(x[j].x, q, one_q, bad), lc);
+                smem[a0 + a1] = fuse<OP>(smem[a0 + a1], A::load_reduce(x[j].y, q, one_q, bad), lc);
             }
         }
+    }
+
+    // u (working array, lazy range) op y (a lazily reduced input word).
+    template <uint32_t OP>
+    __device__ __forceinline__ static W fuse(W u, W y, const LimbConst &lc) {
+        if constexpr (OP == kFuseMul) {
+            return mulmod_lc(u, y, lc);
+        } else {
+            const W q = static_cast<W>(lc.q);
+            const W uc = static_cast<W>(A::canon(u, q)), yc = A::sub_if(y, q);  // both in [0, q)
+            return OP == kFuseAdd ? uc + yc : uc - yc + q;                        // [0, 2q)
+        }
+    }
+
+    // combine<op> for a runtime op (selected once, outside the loop).
+    __device__ __forceinline__ static void combine_op(W *smem, const uint64_t *src, uint32_t rank,
+                                                      const LimbConst &lc, uint32_t &bad, uint32_t op) {
+        if (op == kFuseAdd)
+            combine<kFuseAdd>(smem, src, rank, lc, bad);
+        else if (op == kFuseSub)
+            combine<kFuseSub>(smem, src, rank, lc, bad);
+        else
+            combine<kFuseMul>(smem, src, rank, lc, bad);
     }
 
     __device__ __forceinline__ static W mulmod_lc(W x, W y, const LimbConst &lc) {
@@ -771,7 +797,7 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, fal
     Fwd::prefetch(ring_f, tw, rank);
     __syncthreads();
     Fwd::run(work, tw, lc, rank, ring_f);  // ends with the working array complete
-    Mid::mul(work, a.in2 + base, rank, lc, bad);
+    Mid::template combine<kFuseMul>(work, a.in2 + base, rank, lc, bad);
     typename Inv::Ring ring_i;
     Inv::prefetch(ring_i, tw2, rank);
     __syncthreads();
@@ -782,10 +808,11 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, fal
     }
 }
 
-// Transform and pointwise product fused in one kernel, one cluster per
-// (limb, polynomial), negacyclic plans:
-//   INV = false: C = NTT(A) * B^, the product in the forward's epilogue;
-//   INV = true:  C = INTT(A^ * B^), the product in the inverse's prologue.
+// Transform and pointwise step fused in one kernel, one cluster per
+// (limb, polynomial), negacyclic plans; the step (a.op) is the product, the
+// sum or the difference mod q:
+//   INV = false: C = NTT(A) op B^, the step in the forward's epilogue;
+//   INV = true:  C = INTT(A^ op B^), the step in the inverse's prologue.
 // A^, B^ and the forward's C are in natural order.  B^ is read in the
 // working array's order at the one point where the values sit in that order
 // (after the forward passes, before the inverse passes), as in the fused
@@ -816,12 +843,12 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, fal
     uint32_t bad = 0;
     In::load(work, a.in + base, rank, lc, bad);
     // the thread multiplies the words it has just written: no barrier needed
-    if constexpr (INV) In::mul(work, a.in2 + base, rank, lc, bad);
+    if constexpr (INV) In::combine_op(work, a.in2 + base, rank, lc, bad, a.op);
     typename Tr::Ring ring;
     Tr::prefetch(ring, tw, rank);
     __syncthreads();
     Tr::run(work, tw, lc, rank, ring);  // ends with the working array complete
-    if constexpr (!INV) Out::mul(work, a.in2 + base, rank, lc, bad);
+    if constexpr (!INV) Out::combine_op(work, a.in2 + base, rank, lc, bad, a.op);
     Out::store(work, a.out + base, rank, lc);
     if constexpr (A::kBits == 32) {
         if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) store_status(a.status, kStatusInputRange);

@@ -840,11 +840,24 @@ int bc_poly_mul(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c, u
     return run_coeff(p, kCoeffMul, a, b, c, batch, layout, stream);
 }
 
-// Transform fused with a pointwise product: one launch on the fast kernels
-// (negacyclic plans, 16-byte aligned operands, even strides); otherwise a
-// transform launch and a pointwise launch.
-static int run_ntt_mul(bc_plan *p, bool inverse, const uint64_t *a_, const uint64_t *b, uint64_t *c,
-                       uint32_t batch, const bc_layout *layout, void *stream) {
+// The pointwise step of the fused transforms as its own launch: the product,
+// or the exact sum / difference of the inputs reduced mod q.
+static int pointwise_step(bc_plan *p, uint32_t op, const uint64_t *x, const uint64_t *y, uint64_t *out,
+                          uint32_t batch, const bc_layout *layout, cudaStream_t s) {
+    if (op == kFuseMul) return run_pointwise(p, x, y, out, batch, layout, s);
+    KArgs a;
+    const int st = make_args(p, x, y, out, batch, layout, &a);
+    if (st) return st;
+    return launch_coeff_op(op == kFuseAdd ? kCoeffAddExact : kCoeffSubExact, a, p->degree, p->d_coeff,
+                           CoeffConst{}, s, p->word != Word::W64);
+}
+
+// Transform fused with a pointwise step (kFuseMul / kFuseAdd / kFuseSub):
+// one launch on the fast kernels (negacyclic plans, 16-byte aligned
+// operands, even strides); otherwise a transform launch and a pointwise
+// launch with the same result.
+static int run_ntt_fused(bc_plan *p, bool inverse, uint32_t op, const uint64_t *a_, const uint64_t *b,
+                         uint64_t *c, uint32_t batch, const bc_layout *layout, void *stream) {
     if (!p) return fail(BC_ERR_INVALID_INPUT, "NULL plan");
     KArgs a;
     int st = make_args(p, a_, b, c, batch, layout, &a);
@@ -855,38 +868,59 @@ static int run_ntt_mul(bc_plan *p, bool inverse, const uint64_t *a_, const uint6
     const bool b_aligned = (reinterpret_cast<uintptr_t>(b) & 15u) == 0;
     if (p->kind == KernelKind::Cluster && p->mode == BC_NTT_NEGACYCLIC && fast_layout_ok(a) && b_aligned) {
         a.tw = inverse ? p->d_tw_inv_fast : p->d_tw_fwd_fast;
+        a.op = op;
         return launch_ntt_mul_fast(p->word, inverse, a, s);
     }
-    if (inverse) {  // C = A^ * B^ elementwise (any aliasing), then the inverse in place
-        if ((st = run_pointwise(p, a_, b, c, batch, layout, s))) return st;
+    if (inverse) {  // C = A^ op B^ elementwise (any aliasing), then the inverse in place
+        if ((st = pointwise_step(p, op, a_, b, c, batch, layout, s))) return st;
         return run_inverse(p, c, c, batch, layout, s);
     }
     if (c != b) {
         if ((st = run_forward(p, a_, c, batch, layout, s))) return st;
-        return run_pointwise(p, c, b, c, batch, layout, s);
+        return pointwise_step(p, op, c, b, c, batch, layout, s);
     }
     // C is B^: the forward needs a buffer of its own, laid out like C
     const int64_t ls = a.limb_stride, ps = a.poly_stride;
     const size_t extent = static_cast<size_t>(ls) * (p->n_limbs - 1) + static_cast<size_t>(ps) * (batch - 1) + p->degree;
     void *tmp = nullptr;
     cudaError_t e = cudaMallocFromPoolAsync(&tmp, extent * sizeof(uint64_t), p->ctx->pool, s);
-    if (e != cudaSuccess) return cuda_fail(e, "forward-multiply temporary");
+    if (e != cudaSuccess) return cuda_fail(e, "fused-transform temporary");
     uint64_t *t = static_cast<uint64_t *>(tmp);
     st = run_forward(p, a_, t, batch, layout, s);
-    if (!st) st = run_pointwise(p, t, b, c, batch, layout, s);
+    if (!st) st = pointwise_step(p, op, t, b, c, batch, layout, s);
     e = cudaFreeAsync(tmp, s);
     if (st) return st;
-    return e == cudaSuccess ? BC_OK : cuda_fail(e, "forward-multiply temporary release");
+    return e == cudaSuccess ? BC_OK : cuda_fail(e, "fused-transform temporary release");
 }
 
 int bc_ntt_forward_mul(bc_plan *p, const uint64_t *a, const uint64_t *b_hat, uint64_t *c, uint32_t batch,
                        const bc_layout *layout, void *stream) {
-    return run_ntt_mul(p, false, a, b_hat, c, batch, layout, stream);
+    return run_ntt_fused(p, false, kFuseMul, a, b_hat, c, batch, layout, stream);
 }
 
 int bc_ntt_inverse_mul(bc_plan *p, const uint64_t *a_hat, const uint64_t *b_hat, uint64_t *c, uint32_t batch,
                        const bc_layout *layout, void *stream) {
-    return run_ntt_mul(p, true, a_hat, b_hat, c, batch, layout, stream);
+    return run_ntt_fused(p, true, kFuseMul, a_hat, b_hat, c, batch, layout, stream);
+}
+
+int bc_ntt_forward_add(bc_plan *p, const uint64_t *a, const uint64_t *b_hat, uint64_t *c, uint32_t batch,
+                       const bc_layout *layout, void *stream) {
+    return run_ntt_fused(p, false, kFuseAdd, a, b_hat, c, batch, layout, stream);
+}
+
+int bc_ntt_forward_sub(bc_plan *p, const uint64_t *a, const uint64_t *b_hat, uint64_t *c, uint32_t batch,
+                       const bc_layout *layout, void *stream) {
+    return run_ntt_fused(p, false, kFuseSub, a, b_hat, c, batch, layout, stream);
+}
+
+int bc_ntt_inverse_add(bc_plan *p, const uint64_t *a_hat, const uint64_t *b_hat, uint64_t *c, uint32_t batch,
+                       const bc_layout *layout, void *stream) {
+    return run_ntt_fused(p, true, kFuseAdd, a_hat, b_hat, c, batch, layout, stream);
+}
+
+int bc_ntt_inverse_sub(bc_plan *p, const uint64_t *a_hat, const uint64_t *b_hat, uint64_t *c, uint32_t batch,
+                       const bc_layout *layout, void *stream) {
+    return run_ntt_fused(p, true, kFuseSub, a_hat, b_hat, c, batch, layout, stream);
 }
 
 int bc_polymul(bc_plan *p, const uint64_t *a, const uint64_t *b, uint64_t *c, uint32_t batch,

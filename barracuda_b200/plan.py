@@ -115,6 +115,26 @@ class NttPlan:
         check(lib().bc_ntt_inverse_mul(self.handle, _ptr(a_hat), _ptr(b_hat), _ptr(c), batch,
                                        self._layout(layout), stream or None))
 
+    def forward_add(self, a, b_hat, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
+        """C = NTT(A) + B^ mod q (one fused launch on negacyclic plans)."""
+        check(lib().bc_ntt_forward_add(self.handle, _ptr(a), _ptr(b_hat), _ptr(c), batch,
+                                       self._layout(layout), stream or None))
+
+    def forward_sub(self, a, b_hat, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
+        """C = NTT(A) - B^ mod q (one fused launch on negacyclic plans)."""
+        check(lib().bc_ntt_forward_sub(self.handle, _ptr(a), _ptr(b_hat), _ptr(c), batch,
+                                       self._layout(layout), stream or None))
+
+    def inverse_add(self, a_hat, b_hat, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
+        """C = INTT(A^ + B^ mod q) (one fused launch on negacyclic plans)."""
+        check(lib().bc_ntt_inverse_add(self.handle, _ptr(a_hat), _ptr(b_hat), _ptr(c), batch,
+                                       self._layout(layout), stream or None))
+
+    def inverse_sub(self, a_hat, b_hat, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
+        """C = INTT(A^ - B^ mod q) (one fused launch on negacyclic plans)."""
+        check(lib().bc_ntt_inverse_sub(self.handle, _ptr(a_hat), _ptr(b_hat), _ptr(c), batch,
+                                       self._layout(layout), stream or None))
+
     def poly_add(self, a, b, c, batch: int, layout: Optional[Layout] = None, stream: int = 0):
         check(lib().bc_poly_add(self.handle, _ptr(a), _ptr(b), _ptr(c), batch, self._layout(layout),
                                 stream or None))

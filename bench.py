@@ -573,6 +573,10 @@ KERNEL_CASES = {
     "inverse": (16, 16, "k_ntt_fast", 16),
     "forward_mul": (16, 16, "k_ntt_mul_fast", 24),       # C = NTT(A) * B^
     "inverse_mul": (16, 16, "k_ntt_mul_fast", 24),       # C = INTT(A^ * B^)
+    "forward_add": (16, 16, "k_ntt_mul_fast", 24),       # C = NTT(A) + B^, one launch
+    "inverse_sub": (16, 16, "k_ntt_mul_fast", 24),       # C = INTT(A^ - B^), one launch
+    "forward_then_add": (16, 16, "k_ntt_fast + k_coeff", 24),   # the same as two launches
+    "sub_then_inverse": (16, 16, "k_coeff + k_ntt_fast", 24),
 }
 
 
@@ -620,6 +624,12 @@ def run_kernel_case(args):
         "inverse": lambda: plan.inverse(a, c, batch, stream=sh),
         "forward_mul": lambda: plan.forward_mul(a, b, c, batch, stream=sh),
         "inverse_mul": lambda: plan.inverse_mul(a, b, c, batch, stream=sh),
+        "forward_add": lambda: plan.forward_add(a, b, c, batch, stream=sh),
+        "inverse_sub": lambda: plan.inverse_sub(a, b, c, batch, stream=sh),
+        "forward_then_add": lambda: (plan.forward(a, c, batch, stream=sh),
+                                     plan.poly_add(c, b, c, batch, stream=sh)),
+        "sub_then_inverse": lambda: (plan.poly_sub(a, b, c, batch, stream=sh),
+                                     plan.inverse(c, c, batch, stream=sh)),
     }
     fn = ops[case]
     for _ in range(args.warmup):

@@ -319,6 +319,42 @@ pub mod ffi {
             layout: *const bc_layout,
             stream: *mut c_void,
         ) -> c_int;
+        pub fn bc_ntt_forward_add(
+            plan: *mut bc_plan,
+            d_a: *const u64,
+            d_b_hat: *const u64,
+            d_c: *mut u64,
+            batch: u32,
+            layout: *const bc_layout,
+            stream: *mut c_void,
+        ) -> c_int;
+        pub fn bc_ntt_forward_sub(
+            plan: *mut bc_plan,
+            d_a: *const u64,
+            d_b_hat: *const u64,
+            d_c: *mut u64,
+            batch: u32,
+            layout: *const bc_layout,
+            stream: *mut c_void,
+        ) -> c_int;
+        pub fn bc_ntt_inverse_add(
+            plan: *mut bc_plan,
+            d_a_hat: *const u64,
+            d_b_hat: *const u64,
+            d_c: *mut u64,
+            batch: u32,
+            layout: *const bc_layout,
+            stream: *mut c_void,
+        ) -> c_int;
+        pub fn bc_ntt_inverse_sub(
+            plan: *mut bc_plan,
+            d_a_hat: *const u64,
+            d_b_hat: *const u64,
+            d_c: *mut u64,
+            batch: u32,
+            layout: *const bc_layout,
+            stream: *mut c_void,
+        ) -> c_int;
         pub fn bc_pointwise_mul(
             plan: *mut bc_plan,
             d_a: *const u64,

@@ -270,6 +270,23 @@ int bc_ntt_forward_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b_h
                        uint32_t batch, const bc_layout *layout, void *stream);
 int bc_ntt_inverse_mul(bc_plan *plan, const uint64_t *d_a_hat, const uint64_t *d_b_hat,
                        uint64_t *d_c, uint32_t batch, const bc_layout *layout, void *stream);
+/* Transform fused with FhePolyAdd / FhePolySub (ops/fhe_poly_add.rs:67,
+ * fhe_poly_sub.rs:47), the coefficient-wise steps on either side of it:
+ *   bc_ntt_forward_add / _sub: C = NTT(A) +- B^ mod q, in the forward's epilogue;
+ *   bc_ntt_inverse_add / _sub: C = INTT(A^ +- B^ mod q), in the inverse's prologue.
+ * Exact mod q_l for any input words (A^ and B^ are reduced first; for inputs
+ * below q that is the reference ops' result).  Layouts, aliasing, the
+ * one-launch condition and the input-range report are those of
+ * bc_ntt_forward_mul; otherwise a transform launch and a coefficient launch
+ * give the same result. */
+int bc_ntt_forward_add(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b_hat, uint64_t *d_c,
+                       uint32_t batch, const bc_layout *layout, void *stream);
+int bc_ntt_forward_sub(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b_hat, uint64_t *d_c,
+                       uint32_t batch, const bc_layout *layout, void *stream);
+int bc_ntt_inverse_add(bc_plan *plan, const uint64_t *d_a_hat, const uint64_t *d_b_hat,
+                       uint64_t *d_c, uint32_t batch, const bc_layout *layout, void *stream);
+int bc_ntt_inverse_sub(bc_plan *plan, const uint64_t *d_a_hat, const uint64_t *d_b_hat,
+                       uint64_t *d_c, uint32_t batch, const bc_layout *layout, void *stream);
 /* C = A * B mod q_l, coefficient-wise. */
 int bc_pointwise_mul(bc_plan *plan, const uint64_t *d_a, const uint64_t *d_b, uint64_t *d_c,
                      uint32_t batch, const bc_layout *layout, void *stream);

@@ -394,6 +394,119 @@ def test_forward_mul_fallbacks_and_wide_words(device):
     cplan.close()
 
 
+@pytest.mark.parametrize("logn", [12, 13, 14, 15, 16, 17])
+@pytest.mark.parametrize("bits", [31, 60])
+def test_forward_and_inverse_add_sub_match_the_reference_chain(device, logn, bits):
+    """C = NTT(A) +- B^ and C = INTT(A^ +- B^) in one launch (FhePolyAdd /
+    FhePolySub fused into the transform) equal the reference chain value by
+    value on one polynomial of every limb: the oracle's transform (the
+    reference's algorithm for q < 2^31, exact u128 math above) followed by
+    the reference's coefficient op."""
+    n, limbs, batch = 1 << logn, 2, 2
+    plan, qs, psis = _plan(device, n, limbs, bits, bc.NEGACYCLIC)
+    total = limbs * batch * n
+    a, b, bh, c = (_alloc(device, total) for _ in range(4))
+    plan.fill_uniform(a, batch, seed=13)
+    plan.fill_uniform(b, batch, seed=14)
+    plan.forward(b, bh, batch)  # B^ = NTT(B), canonical
+    device.synchronize()
+    A, Bh = a.to_u64(), bh.to_u64()
+    offs = [(l * batch + 1) * n for l in range(limbs)]
+    Asel = np.concatenate([A[o:o + n] for o in offs])
+    Bsel = np.concatenate([Bh[o:o + n] for o in offs])
+    fwd, inv = (("negacyclic_ntt", "negacyclic_intt") if bits == 31
+                else ("exact_negacyclic_ntt", "exact_negacyclic_intt"))
+    NA = O.batch_transform(fwd, Asel, n, qs, psis)
+    for name, fwd_op, inv_op, coeff in (("add", plan.forward_add, plan.inverse_add, O.ref_poly_add),
+                                        ("sub", plan.forward_sub, plan.inverse_sub, O.ref_poly_sub)):
+        fwd_op(a, bh, c, batch)
+        device.synchronize()
+        C = c.to_u64()
+        for l, o in enumerate(offs):
+            sl = slice(l * n, (l + 1) * n)
+            assert (C[o:o + n] == coeff(NA[sl], Bsel[sl], qs[l])).all(), ("forward", name, l)
+        inv_op(bh, bh if name == "add" else a, c, batch)
+        device.synchronize()
+        C = c.to_u64()
+        other = Bsel if name == "add" else Asel
+        pre = np.concatenate([coeff(Bsel[l * n:(l + 1) * n], other[l * n:(l + 1) * n] % np.uint64(qs[l]), qs[l])
+                              for l in range(limbs)])
+        want = O.batch_transform(inv, pre, n, qs, psis)
+        for l, o in enumerate(offs):
+            assert (C[o:o + n] == want[l * n:(l + 1) * n]).all(), ("inverse", name, l)
+    plan.close()
+
+
+def test_add_sub_fused_aliasing_fallbacks_and_wide_words(device):
+    """C may alias A or B^; cyclic plans and odd strides take the two-launch
+    path with the same result; B^ words in [q, 2^32) are reduced first; a word
+    >= 2^32 on a plan whose moduli are below 2^31 is reported."""
+    n, limbs, batch = 1 << 14, 2, 2
+    plan, qs, _ = _plan(device, n, limbs, 31, bc.NEGACYCLIC)
+    total = limbs * batch * n
+    rng = np.random.default_rng(21)
+    A = rng.integers(0, qs[-1], total, dtype=np.uint64)
+    Bh = rng.integers(0, 2**32, total, dtype=np.uint64)  # not reduced
+    a, bh, c, x = upload(device, A), upload(device, Bh), _alloc(device, total), _alloc(device, total)
+    plan.forward(a, x, batch)
+    plan.forward_sub(a, bh, c, batch)
+    device.synchronize()
+    X, C = x.to_u64(), c.to_u64()
+    for l in range(limbs):
+        sl = slice(l * batch * n, (l + 1) * batch * n)
+        q = np.uint64(qs[l])
+        want = (X[sl] + q - Bh[sl] % q) % q
+        assert (C[sl] == want).all(), l
+    # aliasing: C = A, then C = B^
+    y = upload(device, A)
+    plan.forward_add(y, bh, y, batch)
+    plan.forward_add(a, bh, c, batch)
+    device.synchronize()
+    assert (y.to_u64() == c.to_u64()).all()
+    z = upload(device, Bh)
+    plan.inverse_sub(a, z, z, batch)
+    plan.inverse_sub(a, bh, c, batch)
+    device.synchronize()
+    assert (z.to_u64() == c.to_u64()).all()
+    # cyclic plan: two launches, same result as the device chain
+    cplan, cqs, _ = _plan(device, n, limbs, 31, bc.CYCLIC)
+    cplan.forward(a, x, batch)
+    cplan.forward_add(a, bh, c, batch)
+    device.synchronize()
+    X, C = x.to_u64(), c.to_u64()
+    for l in range(limbs):
+        sl = slice(l * batch * n, (l + 1) * batch * n)
+        q = np.uint64(cqs[l])
+        assert (C[sl] == (X[sl] + Bh[sl] % q) % q).all(), l
+    # odd strides on the negacyclic plan: the two-launch path
+    lay = bc.Layout(limb_stride=batch * (n + 1), poly_stride=n + 1)
+    big = limbs * batch * (n + 1)
+    a2, b2, c2, t2 = (_alloc(device, big) for _ in range(4))
+    plan.fill_uniform(a2, batch, seed=1, layout=lay)
+    plan.fill_uniform(b2, batch, seed=2, layout=lay)
+    plan.inverse_add(a2, b2, c2, batch, layout=lay)
+    plan.poly_add(a2, b2, t2, batch, layout=lay)
+    plan.inverse(t2, t2, batch, layout=lay)
+    device.synchronize()
+    C2, T2 = c2.to_u64(), t2.to_u64()
+    for l in range(limbs):
+        for p in range(batch):
+            o = l * batch * (n + 1) + p * (n + 1)
+            assert (C2[o:o + n] == T2[o:o + n]).all(), (l, p)
+    # a word >= 2^32 in B^ is reported, on both paths
+    bad = Bh.copy()
+    bad[7] = 2**40
+    wb = upload(device, bad)
+    with pytest.raises(bc.BarracudaError):
+        plan.forward_add(a, wb, c, batch)
+        device.synchronize()
+    with pytest.raises(bc.BarracudaError):
+        cplan.inverse_sub(a, wb, c, batch)
+        device.synchronize()
+    cplan.close()
+    plan.close()
+
+
 @pytest.mark.parametrize("logn", [10, 12, 14])
 def test_polymul_shared_memory_path_for_odd_strides(device, logn):
     """Layouts the cluster kernels cannot take (odd strides) route negacyclic
