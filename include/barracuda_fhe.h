@@ -84,7 +84,19 @@ int bc_ctx_device(const bc_ctx *ctx, int *device);
 int bc_ctx_stream(bc_ctx *ctx, void **stream);
 /* Waits for the context stream, then reports (and clears) any status a
  * kernel raised since the last check (e.g. a coefficient >= 2^32 given to a
- * plan whose modulus is below 2^31 -> BC_ERR_INVALID_INPUT). */
+ * plan whose modulus is below 2^31 -> BC_ERR_INVALID_INPUT).
+ *
+ * Which call an input-range error belongs to: kernels raise the status on
+ * the context they were launched for, from any stream, and the next
+ * bc_ctx_sync on that context reports it.  The synchronous reference-op
+ * calls (bc_fhe_*) sync before they return, so their own bad input fails
+ * that call.  The batched plan calls (bc_ntt_*, bc_polymul, ...) are
+ * asynchronous: a bad input in one of them is reported by the first
+ * bc_ctx_sync after its kernels ran, which names no call.  A caller that
+ * must attribute the error syncs after each batched call it wants checked
+ * (or keeps inputs below q, the reference's own domain, where no status is
+ * ever raised).  The kernels still finish: words >= 2^32 are taken modulo
+ * 2^32, so the outputs of a flagged call are not meaningful. */
 int bc_ctx_sync(bc_ctx *ctx);
 
 /* --------------------------------------------------------------- buffers */
