@@ -142,6 +142,37 @@ class ClockSampler:
                 "source": source}
 
 
+def numa_bind(local):
+    """Binds this process's host threads to the CPUs of the NUMA node its GPU
+    hangs off (from sysfs), so that pinned host buffers allocated afterwards
+    are first touched there and host<->device copies do not cross the
+    inter-socket link.  Returns (description for the bench line, previous
+    affinity to restore)."""
+    prev = os.sched_getaffinity(0)
+    try:
+        import torch
+        pr = torch.cuda.get_device_properties(local)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return {"gpu_pci": bus, "numa_node": None, "note": "the system reports no NUMA node"}, prev
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= prev
+        if not cpus:
+            return {"gpu_pci": bus, "numa_node": node, "note": "no allowed CPU on that node"}, prev
+        os.sched_setaffinity(0, cpus)
+        return {"gpu_pci": bus, "numa_node": node, "cpus_bound": len(cpus),
+                "pinned_buffers": "allocated after binding (first touch on the GPU's node)"}, prev
+    except Exception as e:  # no sysfs entry (containers), or no properties
+        return {"note": f"NUMA placement unavailable: {type(e).__name__}: {e}"}, prev
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -311,7 +342,13 @@ def _run_ours(args, torch, bc, group, world, rank, local):
     }
 
     # ---- e2e through the public API with pinned host buffers
-    e2e = (run_e2e(args, torch, plan, lay, polys, x, X, group) if args.e2e_steps > 0 else None)
+    placement, prev_affinity = numa_bind(local)
+    try:
+        e2e = (run_e2e(args, torch, plan, lay, polys, x, X, group) if args.e2e_steps > 0 else None)
+    finally:
+        os.sched_setaffinity(0, prev_affinity)  # the CPU baseline below uses every host core
+    if e2e is not None:
+        e2e["host_placement"] = placement
 
     info = plan.info
     launches_per_transform = {0: 1, 1: 1, 2: N_LOG + 2, 3: 1}[info["kernel_kind"]]
