@@ -39,9 +39,9 @@ METRIC = "negacyclic NTT limb-transforms/s at N=2^16 (fwd+inv, 48 limbs, 128 ct 
 UNIT = "limb-transforms/s"
 # dram__bytes_read.sum + dram__bytes_write.sum of the dominant kernel per
 # limb-transform, from an ncu capture of the forward kernel at 768 transforms
-# per launch ((427.92 + 345.37) MB, `bench.py --cts 8`); DRAM traffic per
+# per launch ((427.93 + 350.64) MB, `bench.py --cts 8`); DRAM traffic per
 # transform does not depend on the batch, so it is scaled to a full launch.
-NCU_TRAFFIC_PER_TRANSFORM = 1_006_895
+NCU_TRAFFIC_PER_TRANSFORM = 1_013_763
 
 
 def peaks():
