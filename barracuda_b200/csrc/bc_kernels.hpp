@@ -80,10 +80,22 @@ int launch_ntt_mul_fast(Word w, bool inverse, const KArgs &a, cudaStream_t s);
 int launch_polymul_fast(Word w, const KArgs &a, cudaStream_t s);
 uint64_t fast_table_index(uint32_t L, int V, uint64_t knat, int pair);
 
-// Multi-pass global-memory path for any N (one launch per stage) through a
-// compact scratch buffer of n_limbs * batch * N words of the plan's width.
+// Stage-per-launch global-memory path for any N through a compact scratch
+// buffer of n_limbs * batch * N words of the plan's width (natural tables):
+// the fallback of cluster plans whose buffers the fast kernels cannot take.
 int launch_ntt_global(Word w, bool gs, bool scale_last, const KArgs &a, void *scratch,
                       cudaStream_t s);
+
+// Two- or three-pass transform of plans above the cluster kernels
+// (bc_kernels_multipass.cu), 2^18 <= N <= 2^24, any layout, through the same
+// kind of scratch buffer.  Its tables store the stages below the TOP pass
+// permuted: natural entry knat sits at multipass_table_index(L, top_lo, knat),
+// top_lo = multipass_top_lo(w, L).
+bool multipass_supported(Word w, uint32_t logn);
+uint32_t multipass_top_lo(Word w, uint32_t logn);
+uint64_t multipass_table_index(uint32_t L, uint32_t top_lo, uint64_t knat);
+int launch_ntt_multipass(Word w, bool gs, bool scale_last, const KArgs &a, void *scratch,
+                         cudaStream_t s);
 
 // C = A * B mod q per coefficient (exact; inputs < 2^32 for 32-bit words).
 int launch_pointwise(Word w, const KArgs &a, cudaStream_t s);

@@ -310,7 +310,8 @@ int run_global(bc_plan *p, bool gs, bool inverse, const KArgs &a, uint32_t batch
     void *scratch = nullptr;
     cudaError_t e = cudaMallocFromPoolAsync(&scratch, need, p->ctx->pool, s);
     if (e != cudaSuccess) return cuda_fail(e, "transform scratch");
-    const int st = launch_ntt_global(p->word, gs, inverse, a, scratch, s);
+    const int st = p->kind == KernelKind::Global ? launch_ntt_multipass(p->word, gs, inverse, a, scratch, s)
+                                                 : launch_ntt_global(p->word, gs, inverse, a, scratch, s);
     e = cudaFreeAsync(scratch, s);
     if (st) return st;
     return e == cudaSuccess ? BC_OK : cuda_fail(e, "transform scratch release");
@@ -685,6 +686,23 @@ int bc_plan_create(bc_ctx *ctx, uint32_t degree, uint32_t n_limbs, const uint64_
     if ((st = use_device(ctx))) {
         delete p;
         return st;
+    }
+    // the multi-pass kernels (every plan above the cluster kernels) read the
+    // stages below their TOP pass permuted
+    if (p->kind == KernelKind::Global) {
+        const size_t entry = p->word == Word::W64 ? 16 : 8;
+        const uint64_t N = degree;
+        const uint32_t top_lo = multipass_top_lo(p->word, p->logn);
+        std::vector<unsigned char> tmp(entry * N);
+        for (std::vector<unsigned char> *t : {&fwd, &inv}) {
+            for (uint32_t l = 0; l < n_limbs; ++l) {
+                unsigned char *base = t->data() + entry * N * l;
+                std::memcpy(tmp.data(), base, tmp.size());
+                for (uint64_t k = 1; k < N; ++k)
+                    std::memcpy(base + entry * multipass_table_index(p->logn, top_lo, k), tmp.data() + entry * k,
+                                entry);
+            }
+        }
     }
     // the fast kernels read each direction's table in their own layout
     std::vector<unsigned char> fwd_fast, inv_fast, gs_fast;

@@ -87,7 +87,7 @@ int transform(bc_plan *p, bool inverse, const uint64_t *in, uint64_t *out, uint3
         if (p->logn <= smem_max_logn(p->word)) return launch_ntt_smem(p->word, gs, inverse, a, s);
         return launch_ntt_global(p->word, gs, inverse, a, glb, s);
     case KernelKind::Smem: return launch_ntt_smem(p->word, gs, inverse, a, s);
-    default: return launch_ntt_global(p->word, gs, inverse, a, glb, s);
+    default: return launch_ntt_multipass(p->word, gs, inverse, a, glb, s);
     }
 }
 

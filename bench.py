@@ -459,6 +459,57 @@ def run_e2e(args, torch, plan, lay, polys, x, X, group):
             "timing": "CUDA events around the copy/compute streams, max over ranks"}
 
 
+def run_sweep_large(args):
+    """N = 2^18 .. 2^24 on one GPU, both prime families: forward and inverse
+    of 4 limbs x a batch of about 1 GiB (u64) per buffer through the
+    multi-pass kernels.  One JSON line per (bits, N): launch times, limb-
+    transforms/s, and GB/s as 16N algorithmic bytes per limb-transform (the
+    passes move 24N bytes at 2^18 with 32-bit words, 32N otherwise).  Not the
+    headline bench line; --sweep-large selects it."""
+    import torch
+
+    import barracuda_b200 as bc
+
+    torch.cuda.set_device(0)
+    dev = bc.Device(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sh = stream.cuda_stream
+    hbm, peak_kind = peaks()
+    for bits in (31, 60):
+        for L in range(18, 25):
+            n, limbs = 1 << L, 4
+            batch = max(1, (1 << 27) // (n * limbs))
+            qs = bc.ntt_primes(bits, n, limbs)
+            plan = bc.NttPlan(dev, n, qs, [bc.negacyclic_root(q, n) for q in qs], mode=bc.NEGACYCLIC)
+            x = torch.empty(limbs * batch * n, dtype=torch.int64, device="cuda")
+            y, z = torch.empty_like(x), torch.empty_like(x)
+            plan.fill_uniform(x, batch, seed=1, stream=sh)
+            line = {"sweep": "large N, multi-pass kernels, 1 GPU", "N": n, "bits": bits, "limbs": limbs,
+                    "batch": batch, "passes": 2 if (bits < 32 and L == 18) else 3,
+                    "peak_gbs": hbm, "peak_kind": peak_kind}
+            for name, fn, src, dst in (("forward", plan.forward, x, y), ("inverse", plan.inverse, y, z)):
+                for _ in range(args.warmup):
+                    fn(src, dst, batch, stream=sh)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record(stream)
+                for _ in range(args.steps):
+                    fn(src, dst, batch, stream=sh)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / args.steps
+                units = limbs * batch
+                gbs = units * 16 * n / (ms / 1000.0) / 1e9
+                line[name] = {"ms": ms, "limb_transforms_per_s": units / (ms / 1000.0), "gb_per_s": gbs,
+                              "frac": gbs / hbm}
+            line["round_trip_exact"] = bool(torch.equal(x, z))
+            print(json.dumps(line), flush=True)
+            del x, y, z
+            plan.close()
+    dev.close()
+
+
 def run_sweep(args):
     """Config 4: for each N, forward and inverse of a [limb][poly][N] batch of
     about 2 GiB (u64) per GPU, sharded by limb across the ranks (each GPU
@@ -614,6 +665,8 @@ KERNEL_CASES = {
     "inverse_sub": (16, 16, "k_ntt_mul_fast", 24),       # C = INTT(A^ - B^), one launch
     "forward_then_add": (16, 16, "k_ntt_fast + k_coeff", 24),   # the same as two launches
     "sub_then_inverse": (16, 16, "k_coeff + k_ntt_fast", 24),
+    "forward_large": (20, 4, "k_ntt_pass", 16),          # N = 2^20: three multi-pass launches
+    "inverse_large": (20, 4, "k_ntt_pass", 16),
 }
 
 
@@ -659,6 +712,8 @@ def run_kernel_case(args):
         "decompose": lambda: bc.decompose(dev, a, c, words, 1 << 16, 3, stream=sh),
         "forward": lambda: plan.forward(a, c, batch, stream=sh),
         "inverse": lambda: plan.inverse(a, c, batch, stream=sh),
+        "forward_large": lambda: plan.forward(a, c, batch, stream=sh),
+        "inverse_large": lambda: plan.inverse(a, c, batch, stream=sh),
         "forward_mul": lambda: plan.forward_mul(a, b, c, batch, stream=sh),
         "inverse_mul": lambda: plan.inverse_mul(a, b, c, batch, stream=sh),
         "forward_add": lambda: plan.forward_add(a, b, c, batch, stream=sh),
@@ -778,6 +833,8 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="per-N forward/inverse report (config 4 shape) instead of the bench line")
+    ap.add_argument("--sweep-large", action="store_true",
+                    help="per-N forward/inverse report for N = 2^18..2^24 (multi-pass kernels)")
     ap.add_argument("--op-latency", action="store_true",
                     help="single-call latency of the reference op API at N=4096 (not a bench line)")
     ap.add_argument("--kernel-case", choices=sorted(KERNEL_CASES),
@@ -791,6 +848,8 @@ def main(argv=None):
         run_op_latency(args)
     elif args.sweep:
         run_sweep(args)
+    elif args.sweep_large:
+        run_sweep_large(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

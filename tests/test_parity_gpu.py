@@ -534,24 +534,86 @@ def _exact_negacyclic(x, n, q, psi):
     return out
 
 
-@pytest.mark.parametrize("logn,bits", [(18, 31), (18, 60), (19, 31)])
-def test_plan_multipass_global_path(device, logn, bits):
-    """N above the cluster kernels: one launch per stage through a per-call
-    temporary; exact forward values and the round trip."""
+# N = 2^18 .. 2^24 run on the two-pass (2^18, 32-bit words) and three-pass
+# kernels; 30-bit primes take the [0, 4q) word flavour, 31-bit [0, 2q), 60-bit
+# the 64-bit words.
+MULTIPASS_CASES = [(18, 31), (18, 30), (18, 60), (19, 31), (19, 60), (20, 31), (20, 30), (21, 60),
+                   (22, 31), (23, 60), (24, 31), (24, 60)]
+
+
+def _exact_cyclic_inverse(y, n, q, w):
+    """N^-1 * NTT_{w^-1}(y), exact (oracle)."""
+    t = O.exact_ntt(y, n, q, pow(w, -1, q))
+    return O.exact_poly_mul(t, np.full(n, pow(n, -1, q), dtype=np.uint64), q)
+
+
+@pytest.mark.parametrize("logn,bits", MULTIPASS_CASES)
+@pytest.mark.parametrize("mode", [bc.NEGACYCLIC, bc.CYCLIC])
+def test_plan_multipass_matches_oracle(device, logn, bits, mode):
+    """N above the cluster kernels: exact forward and inverse values on the
+    first and the last limb-polynomial of the batch, and the round trip of
+    every one."""
     n, limbs, batch = 1 << logn, 2, 2
-    plan, qs, psis = _plan(device, n, limbs, bits, bc.NEGACYCLIC)
+    plan, qs, roots = _plan(device, n, limbs, bits, mode)
     assert plan.info["kernel_kind"] == 2
     total = limbs * batch * n
-    src, dst, back = _alloc(device, total), _alloc(device, total), _alloc(device, total)
-    plan.fill_uniform(src, batch, seed=logn)
+    src, dst, back, inv = (_alloc(device, total) for _ in range(4))
+    plan.fill_uniform(src, batch, seed=logn + bits)
     plan.forward(src, dst, batch)
     plan.inverse(dst, back, batch)
+    plan.inverse(src, inv, batch)
     device.synchronize()
-    x, X = src.to_u64(), dst.to_u64()
+    x, X, Y = src.to_u64(), dst.to_u64(), inv.to_u64()
     assert (back.to_u64() == x).all()
-    for l, p in ((0, 0), (1, batch - 1)):
+    # the oracle takes ~8 s per transform at 2^24: one polynomial from 2^22 up
+    for l, p in ((0, 0), (1, batch - 1)) if logn < 22 else ((1, batch - 1),):
         off = (l * batch + p) * n
-        assert (X[off:off + n] == _exact_negacyclic(x[off:off + n], n, qs[l], psis[l])).all(), (l, p)
+        xs, q, r = x[off:off + n], qs[l], roots[l]
+        if mode == bc.NEGACYCLIC:
+            want_f = O.exact_negacyclic_ntt(xs, n, q, r)
+            want_i = O.exact_negacyclic_intt(xs, n, q, r)
+        else:
+            want_f = O.exact_ntt(xs, n, q, r)
+            want_i = _exact_cyclic_inverse(xs, n, q, r)
+        assert (X[off:off + n] == want_f).all(), ("forward", l, p)
+        assert (Y[off:off + n] == want_i).all(), ("inverse", l, p)
+    plan.close()
+
+
+@pytest.mark.parametrize("logn,bits", [(18, 31), (20, 60), (21, 31)])
+def test_plan_multipass_layouts(device, logn, bits):
+    """The multi-pass kernels take any layout: padded strides, limbs not
+    adjacent, unaligned pointers and in-place calls give the compact
+    layout's results."""
+    n, limbs, batch = 1 << logn, 2, 2
+    plan, qs, psis = _plan(device, n, limbs, bits, bc.NEGACYCLIC)
+    total = limbs * batch * n
+    src, want = _alloc(device, total), _alloc(device, total)
+    plan.fill_uniform(src, batch, seed=7)
+    plan.forward(src, want, batch)
+    device.synchronize()
+    x, W = src.to_u64(), want.to_u64()
+    pad, gap = 3, 5  # words after each polynomial, words between limbs
+    lay = bc.Layout(limb_stride=batch * (n + pad) + gap, poly_stride=n + pad)
+    words = limbs * lay.limb_stride + 1
+    big_in, big_out = _alloc(device, words), _alloc(device, words)
+    host = np.zeros(words, dtype=np.uint64)
+    for l in range(limbs):
+        for p in range(batch):
+            o = 1 + l * lay.limb_stride + p * lay.poly_stride  # one word in: 8-byte aligned only
+            host[o:o + n] = x[(l * batch + p) * n:(l * batch + p + 1) * n]
+    N.check(N.lib().bc_buf_h2d(device.handle, big_in.ptr, host.ctypes.data, host.nbytes))
+    base_in, base_out = big_in.ptr + 8, big_out.ptr + 8
+    plan.forward(base_in, base_out, batch, layout=lay)
+    plan.forward(base_in, base_in, batch, layout=lay)  # in place
+    device.synchronize()
+    out, inplace = big_out.to_u64(), big_in.to_u64()
+    for l in range(limbs):
+        for p in range(batch):
+            o = 1 + l * lay.limb_stride + p * lay.poly_stride
+            ref = W[(l * batch + p) * n:(l * batch + p + 1) * n]
+            assert (out[o:o + n] == ref).all(), (l, p)
+            assert (inplace[o:o + n] == ref).all(), (l, p)
     plan.close()
 
 
