@@ -44,30 +44,30 @@ int check_launch_mp(const char *what) {
                 format("%s launch failed: %s", what, cudaGetErrorString(e)));
 }
 
-template <class A, bool GS, int S, int ROLE>
-int launch_pass(const KArgs &a, void *scratch, uint32_t lo, int scale, cudaStream_t s) {
+template <class A, bool GS, bool SCALE, int S, int ROLE>
+int launch_pass(const KArgs &a, void *scratch, uint32_t lo, cudaStream_t s) {
     using W = typename A::W;
     const size_t smem = sizeof(W) * (32u << S);
-    static const cudaError_t attr = cudaFuncSetAttribute(mp::k_ntt_pass<A, GS, S, ROLE>,
+    static const cudaError_t attr = cudaFuncSetAttribute(mp::k_ntt_pass<A, GS, SCALE, S, ROLE>,
                                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                          static_cast<int>(smem));
     if (attr != cudaSuccess) return cuda_fail(attr, "multi-pass transform shared memory");
     const uint32_t tile_bits = ROLE == mp::kTop ? lo - 5 : a.logn - 5 - S;
     const uint64_t blocks = (static_cast<uint64_t>(a.batch) * a.n_limbs) << tile_bits;
     if (blocks > 0x7FFFFFFFull) return fail(BC_ERR_UNSUPPORTED, "batch too large for the multi-pass transform");
-    mp::k_ntt_pass<A, GS, S, ROLE><<<static_cast<unsigned>(blocks), mp::kThreads, smem, s>>>(
-        a, static_cast<W *>(scratch), lo, scale);
+    mp::k_ntt_pass<A, GS, SCALE, S, ROLE><<<static_cast<unsigned>(blocks), mp::kThreads, smem, s>>>(
+        a, static_cast<W *>(scratch), lo);
     return check_launch_mp("k_ntt_pass");
 }
 
-template <class A, bool GS, int ROLE>
-int launch_pass_s(int S, const KArgs &a, void *scratch, uint32_t lo, int scale, cudaStream_t s) {
+template <class A, bool GS, bool SCALE, int ROLE>
+int launch_pass_s(int S, const KArgs &a, void *scratch, uint32_t lo, cudaStream_t s) {
     switch (S) {
-    case 6: return launch_pass<A, GS, 6, ROLE>(a, scratch, lo, scale, s);
-    case 7: return launch_pass<A, GS, 7, ROLE>(a, scratch, lo, scale, s);
-    case 8: return launch_pass<A, GS, 8, ROLE>(a, scratch, lo, scale, s);
+    case 6: return launch_pass<A, GS, SCALE, 6, ROLE>(a, scratch, lo, s);
+    case 7: return launch_pass<A, GS, SCALE, 7, ROLE>(a, scratch, lo, s);
+    case 8: return launch_pass<A, GS, SCALE, 8, ROLE>(a, scratch, lo, s);
     case 9:
-        if constexpr (A::kBits == 32) return launch_pass<A, GS, 9, ROLE>(a, scratch, lo, scale, s);
+        if constexpr (A::kBits == 32) return launch_pass<A, GS, SCALE, 9, ROLE>(a, scratch, lo, s);
         [[fallthrough]];
     default: return fail(BC_ERR_INTERNAL, format("no multi-pass tile of %d bits", S));
     }
@@ -83,14 +83,15 @@ int run_passes(const KArgs &a, void *scratch, bool scale, cudaStream_t s, Word w
     for (int k = 0; k < sc.n; ++k) {
         const int p = GS ? k : sc.n - 1 - k;  // CT from the top bits down, GS from the bottom up
         // N^-1 rides on the last stage executed: GS b = L-1 (TOP), CT b = 0 (LOW)
-        const int sc_flag = scale && (GS ? p == top : p == 0) ? 1 : 0;
         int st;
         if (p == top)
-            st = launch_pass_s<A, GS, mp::kTop>(sc.bits[p], a, scratch, lo[p], sc_flag, s);
+            st = GS && scale ? launch_pass_s<A, GS, true, mp::kTop>(sc.bits[p], a, scratch, lo[p], s)
+                             : launch_pass_s<A, GS, false, mp::kTop>(sc.bits[p], a, scratch, lo[p], s);
         else if (p == 0)
-            st = launch_pass_s<A, GS, mp::kLow>(sc.bits[p], a, scratch, lo[p], sc_flag, s);
+            st = !GS && scale ? launch_pass_s<A, GS, true, mp::kLow>(sc.bits[p], a, scratch, lo[p], s)
+                              : launch_pass_s<A, GS, false, mp::kLow>(sc.bits[p], a, scratch, lo[p], s);
         else
-            st = launch_pass_s<A, GS, mp::kMid>(sc.bits[p], a, scratch, lo[p], sc_flag, s);
+            st = launch_pass_s<A, GS, false, mp::kMid>(sc.bits[p], a, scratch, lo[p], s);
         if (st) return st;
     }
     return BC_OK;

@@ -43,17 +43,30 @@ enum Role : int { kTop = 0, kMid = 1, kLow = 2 };
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
-// Register rounds of a pass of S bits, from the lowest bits up: widths of
-// at most 3 bits, each leaving at least 8 tasks (one per warp).
-__host__ __device__ constexpr int round_count(int S) { return S <= 6 ? 2 : 3; }
-__host__ __device__ constexpr int round_width(int S, int r) {
-    // S = 6: 3 3 / 7: 2 2 3 / 8: 2 3 3 / 9: 3 3 3
-    return S == 6 ? 3 : S == 7 ? (r == 2 ? 3 : 2) : S == 8 ? (r == 0 ? 2 : 3) : 3;
+// Register rounds of a pass of S bits for words of WB bytes, from the lowest
+// bits up, each leaving at least 8 tasks (one per warp).  32-bit words: two
+// rounds of floor(S/2) and ceil(S/2) bits (radix 8 or 16 in registers) for
+// S <= 8, three rounds of 3 bits for S = 9.  64-bit words, twice the
+// registers per coefficient: rounds of at most 3 bits.
+__host__ __device__ constexpr int round_count(int S, int WB) { return (S == 9 || (WB == 8 && S > 6)) ? 3 : 2; }
+__host__ __device__ constexpr int round_width(int S, int WB, int r) {
+    return round_count(S, WB) == 2 ? (r == 0 ? S / 2 : S - S / 2) : (S == 9 ? 3 : (r == 0 ? 2 : (S == 7 && r == 1 ? 2 : 3)));
 }
-__host__ __device__ constexpr int round_lo(int S, int r) {
+__host__ __device__ constexpr int round_lo(int S, int WB, int r) {
     int lo = 0;
-    for (int i = 0; i < r; ++i) lo += round_width(S, i);
+    for (int i = 0; i < r; ++i) lo += round_width(S, WB, i);
     return lo;
+}
+
+// CTAs per SM a pass is compiled for (register budget 65536 / (256 x this)):
+// as many as its tile allows in shared memory (228 KB per SM) where the
+// largest round still fits without spills (ptxas -v), fewer otherwise.
+template <class A, int S>
+__host__ __device__ constexpr int min_blocks() {
+    if constexpr (sizeof(typename A::W) == 4)
+        return S == 6 ? 6 : S == 7 ? 5 : S == 8 ? 4 : 3;  // 40 / 48 / 64 / 80 registers
+    else
+        return S == 8 ? 3 : 4;  // 64 / 64 / 80 registers
 }
 
 // Shared-memory word of tile element (row, col); TOP tiles swizzle the
@@ -70,93 +83,111 @@ struct Ctx {
     uint32_t L, lo;
     uint32_t t;           // tile index within the polynomial
     uint32_t lane, warp;
-    int scale;            // fold N^-1 into the transform's last stage
+    uint32_t pfix;        // MID / LOW: the tile's fixed position bits (t placed around the pass)
+    uint32_t blk0;        // MID / LOW: N >> (lo + 1), table block of the pass's lowest stage
+    uint32_t pf0;         // MID / LOW: pfix >> (lo + 1)
 };
 
-template <class A>
-__device__ __forceinline__ void bfly(bool gs, bool scaled, typename A::W &x, typename A::W &y,
-                                     const typename A::Tw &w, const LimbConst &lc) {
+template <class A, bool GS, bool SCALED>
+__device__ __forceinline__ void bfly(typename A::W &x, typename A::W &y, const typename A::Tw &w,
+                                     const LimbConst &lc) {
     using W = typename A::W;
     const W q = static_cast<W>(lc.q);
-    if (scaled) {
+    if constexpr (SCALED) {
         const W s = static_cast<W>(lc.ninv), sq = static_cast<W>(lc.ninv_shoup);
-        if (gs)
+        if constexpr (GS)
             A::gs_scaled(x, y, w.x, w.y, s, sq, q);
         else
             A::ct_scaled(x, y, w.x, w.y, s, sq, q);
     } else {
-        if (gs)
+        if constexpr (GS)
             A::gs(x, y, w.x, w.y, q);
         else
             A::ct(x, y, w.x, w.y, q);
     }
 }
 
+// Stage J of a round: the butterflies of register pairs (m, m | 2^J).
+// Whether N^-1 rides on it is known at compile time: the transform's last
+// stage is GS b = L - 1 (the TOP pass's highest row bit) or CT b = 0 (the
+// LOW pass's lowest).  Table entry of register 0 for stage b = lo + RR + J:
+//   TOP:       (N >> (b+1)) + (row >> (RR+J+1)), natural layout;
+//   MID / LOW: (N >> (b+1)) + (((p >> (b+1)) mod 2^(L-b-6)) << 5) + lane, the
+//              sigma layout, where p >> (b+1) without the column is
+//              (pfix >> (b+1)) | (row >> (RR+J+1)).
+// Register m reads (m >> (J+1)) entries (TOP) or rows of 32 entries further.
+template <class A, bool GS, bool SCALE, int S, int ROLE, int RR, int K, int J>
+__device__ __forceinline__ void round_stage(typename A::W (&v)[1 << K], const typename A::Tw *tw, uint32_t base,
+                                            const Ctx &c, const LimbConst &lc) {
+    constexpr bool kScaled =
+        SCALE && (GS ? (ROLE == kTop && RR + J == S - 1) : (ROLE == kLow && RR + J == 0));
+    constexpr int kStride = ROLE == kTop ? 1 : 32;
+    const typename A::Tw *tb;
+    if constexpr (ROLE == kTop)
+        tb = tw + ((1u << (S - RR - J - 1)) + (base >> (RR + J + 1)));
+    else
+        tb = tw + c.lane + (c.blk0 >> (RR + J)) + (((c.pf0 >> (RR + J)) | (base >> (RR + J + 1))) << 5);
+#pragma unroll
+    for (int m = 0; m < (1 << K); ++m) {
+        if (m & (1 << J)) continue;
+        const typename A::Tw w = __ldg(tb + (m >> (J + 1)) * kStride);
+        bfly<A, GS, kScaled>(v[m], v[m | (1 << J)], w, lc);
+    }
+}
+
+template <class A, bool GS, bool SCALE, int S, int ROLE, int RR, int K, int JJ>
+__device__ __forceinline__ void round_stages(typename A::W (&v)[1 << K], const typename A::Tw *tw, uint32_t base,
+                                             const Ctx &c, const LimbConst &lc) {
+    // CT runs a round's stages from its top bit down, GS from its bottom up
+    round_stage<A, GS, SCALE, S, ROLE, RR, K, GS ? JJ : K - 1 - JJ>(v, tw, base, c, lc);
+    if constexpr (JJ + 1 < K) round_stages<A, GS, SCALE, S, ROLE, RR, K, JJ + 1>(v, tw, base, c, lc);
+}
+
 // One register round: bits [RR, RR + K) of the row (absolute position bits
 // lo + RR ..).  Each thread runs the round's K stages on 2^K coefficients of
-// its column (= lane) per task; a task fixes the row's other bits.
-template <class A, bool GS, int S, int ROLE, int RR, int K>
+// its column (= lane) per task; a task fixes the row's other bits.  Shared-
+// memory addresses are a per-task base plus compile-time offsets.
+template <class A, bool GS, bool SCALE, int S, int ROLE, int RR, int K>
 __device__ __forceinline__ void pass_round(typename A::W *tile, const typename A::Tw *tw, const LimbConst &lc,
-                                      const Ctx &c) {
+                                           const Ctx &c) {
     using W = typename A::W;
-    using Tw = typename A::Tw;
     constexpr int kTasks = 1 << (S - K);
     constexpr int kPer = kTasks / kWarps;
     static_assert(kPer >= 1, "a round must give every warp a task");
-    const uint32_t L = c.L;
-    // Position bits of this tile other than the pass's rows and the column
-    // (MID / LOW: t splits around the pass's bits; TOP: t is bits [5, lo)).
-    const uint32_t t_lo = c.t & ((1u << c.lo) - 1u), t_hi = c.t >> c.lo;
+    constexpr int TB = S - 5;  // TOP: the row's top five bits swizzle the column
 #pragma unroll 1
     for (int it = 0; it < kPer; ++it) {
         const uint32_t g = c.warp + kWarps * it;
-        const uint32_t base = ((g >> RR) << (RR + K)) | (g & ((1u << RR) - 1u));
+        const uint32_t base = ((g >> RR) << (RR + K)) | (g & ((1u << RR) - 1u));  // round bits zero
+        // word of (base, lane); register m adds row m << RR
+        const uint32_t lx = ROLE == kTop ? (c.lane ^ (base >> TB)) : c.lane;
+        W *const t0 = tile + base * 32u;
         W v[1 << K];
 #pragma unroll
         for (int m = 0; m < (1 << K); ++m) {
-            const uint32_t row = base | (static_cast<uint32_t>(m) << RR);
-            v[m] = tile[tile_addr<S, ROLE>(row, c.lane)];
+            const uint32_t mr = static_cast<uint32_t>(m) << RR;
+            v[m] = t0[mr * 32u + (ROLE == kTop ? (lx ^ (mr >> TB)) : lx)];
         }
-#pragma unroll
-        for (int jj = 0; jj < K; ++jj) {
-            const int j = GS ? jj : K - 1 - jj;
-            const uint32_t b = c.lo + RR + j;
-            const bool scaled = c.scale && b == (GS ? L - 1 : 0u);
-            // table block of stage b and this task's entry for m = 0
-            const Tw *tb;
-            if constexpr (ROLE == kTop) {
-                tb = tw + ((1u << (L - b - 1)) + (base >> (RR + j + 1)));
-            } else {
-                const uint32_t pn = (t_hi << (c.lo + S)) | (base << c.lo) | t_lo;  // p without the column
-                const uint32_t mask = (1u << (L - b - 6)) - 1u;
-                tb = tw + ((1u << (L - b - 1)) + (((pn >> (b + 1)) & mask) << 5) + c.lane);
-            }
-            constexpr int kStride = ROLE == kTop ? 1 : 32;
-#pragma unroll
-            for (int m = 0; m < (1 << K); ++m) {
-                if (m & (1 << j)) continue;
-                const Tw w = __ldg(tb + (m >> (j + 1)) * kStride);
-                bfly<A>(GS, scaled, v[m], v[m | (1 << j)], w, lc);
-            }
-        }
+        round_stages<A, GS, SCALE, S, ROLE, RR, K, 0>(v, tw, base, c, lc);
 #pragma unroll
         for (int m = 0; m < (1 << K); ++m) {
-            const uint32_t row = base | (static_cast<uint32_t>(m) << RR);
-            tile[tile_addr<S, ROLE>(row, c.lane)] = v[m];
+            const uint32_t mr = static_cast<uint32_t>(m) << RR;
+            t0[mr * 32u + (ROLE == kTop ? (lx ^ (mr >> TB)) : lx)] = v[m];
         }
     }
 }
 
-template <class A, bool GS, int S, int ROLE, int R>
+template <class A, bool GS, bool SCALE, int S, int ROLE, int R>
 __device__ __forceinline__ void rounds_from(typename A::W *tile, const typename A::Tw *tw, const LimbConst &lc,
                                             const Ctx &c) {
     // CT runs the rounds from the top bits down, GS from the bottom up.
-    constexpr int NR = round_count(S);
+    constexpr int WB = static_cast<int>(sizeof(typename A::W));
+    constexpr int NR = round_count(S, WB);
     constexpr int r = GS ? R : NR - 1 - R;
-    pass_round<A, GS, S, ROLE, round_lo(S, r), round_width(S, r)>(tile, tw, lc, c);
+    pass_round<A, GS, SCALE, S, ROLE, round_lo(S, WB, r), round_width(S, WB, r)>(tile, tw, lc, c);
     if constexpr (R + 1 < NR) {
         __syncthreads();
-        rounds_from<A, GS, S, ROLE, R + 1>(tile, tw, lc, c);
+        rounds_from<A, GS, SCALE, S, ROLE, R + 1>(tile, tw, lc, c);
     }
 }
 
@@ -170,9 +201,8 @@ __device__ __forceinline__ void flag_bad(uint32_t *status, uint32_t bad) {
 // LOW (reads bit-reversed input) .. MID .. TOP (writes natural output).
 // Every other side is the sigma-order scratch (lazy residues of the plan's
 // word width).
-template <class A, bool GS, int S, int ROLE>
-__global__ void __launch_bounds__(kThreads) k_ntt_pass(KArgs a, typename A::W *scratch, uint32_t lo,
-                                                       int scale) {
+template <class A, bool GS, bool SCALE, int S, int ROLE>
+__global__ void __launch_bounds__(kThreads, (min_blocks<A, S>())) k_ntt_pass(KArgs a, typename A::W *scratch, uint32_t lo) {
     using W = typename A::W;
     using Tw = typename A::Tw;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -186,7 +216,9 @@ __global__ void __launch_bounds__(kThreads) k_ntt_pass(KArgs a, typename A::W *s
     c.t = blockIdx.x & ((1u << tile_bits) - 1u);
     c.lane = threadIdx.x & 31u;
     c.warp = threadIdx.x >> 5;
-    c.scale = scale;
+    c.pfix = ROLE == kTop ? 0u : (((c.t >> lo) << (lo + S)) | (c.t & ((1u << lo) - 1u)));
+    c.blk0 = 1u << (L - lo - 1);
+    c.pf0 = c.pfix >> (lo + 1);
     const uint32_t limb = static_cast<uint32_t>(pl / a.batch), poly = static_cast<uint32_t>(pl % a.batch);
     const LimbConst lc = a.limbs[limb];
     const W q = static_cast<W>(lc.q);
@@ -197,75 +229,75 @@ __global__ void __launch_bounds__(kThreads) k_ntt_pass(KArgs a, typename A::W *s
     const bool writes_user = GS ? ROLE == kTop : ROLE == kLow;
     constexpr int kPerThread = (32 << S) / kThreads;  // tile elements per thread
     constexpr int kBatch = 8;
-    const uint32_t t_lo = c.t & ((1u << lo) - 1u), t_hi = c.t >> lo;
+    constexpr int TB = S - 5;
+
+    // Element i (0 <= i < kPerThread) of this thread on each side of the
+    // pass, as a per-thread base plus a per-i step (every field below is
+    // disjoint in bits, so ORs are adds and XORs distribute):
+    //   TOP, natural (lanes = columns): row = warp + 8i, global index
+    //     (row << lo) | (t << 5) | lane, word row * 32 + (lane ^ (row >> TB));
+    //   TOP, sigma (lanes = the row's top five bits): row = (lane << TB) | (i >> 2),
+    //     column warp | 8(i & 3), sigma index (i >> 2) << (lo + 5) | t << 10 | column << 5 | lane;
+    //   MID / LOW, sigma: row = warp + 8i, sigma index pfix << 5 | row << (lo + 5) | lane;
+    //   LOW, bit-reversed (lane l takes column bitrev5(l)): row = warp + 8i, global
+    //     index bitrev_L(column << (L-5) | t << S | row) = kb | bitrev_L(8i).
+    const uint32_t lane = c.lane, warp = c.warp;
+    const uint32_t col_r = __brev(lane) >> 27;
+    const unsigned long long *uin = reinterpret_cast<const unsigned long long *>(a.in) + ubase;
+    unsigned long long *uout = reinterpret_cast<unsigned long long *>(a.out) + ubase;
+    const uint64_t nat_base = (static_cast<uint64_t>(warp) << lo) | (c.t << 5) | lane;
+    const uint64_t nat_step = static_cast<uint64_t>(kWarps) << lo;
+    const uint32_t nat_lx = lane ^ (warp >> TB);
+    const uint64_t sgt_base = (static_cast<uint64_t>(c.t) << 10) | (warp << 5) | lane;
+    const uint64_t sgt_step = 1ull << (lo + 5);
+    const uint32_t sgt_s0 = (lane << (TB + 5)), sgt_wl = warp ^ lane;
+    const uint64_t sg_base = (static_cast<uint64_t>(c.pfix) << 5) | (static_cast<uint64_t>(warp) << (lo + 5)) | lane;
+    const uint64_t sg_step = static_cast<uint64_t>(kWarps) << (lo + 5);
+    const uint32_t br_kb = __brev((col_r << (L - 5)) | (c.t << S) | warp) >> (32 - L);
+    const uint32_t br_sh = 32 - L;
+    auto nat_g = [&](int i) { return nat_base + static_cast<uint64_t>(i) * nat_step; };
+    auto nat_s = [&](int i) { return (warp + kWarps * i) * 32u + (nat_lx ^ ((kWarps * i) >> TB)); };
+    auto sgt_g = [&](int i) {
+        return sgt_base + static_cast<uint64_t>(i >> 2) * sgt_step + (static_cast<uint64_t>(kWarps * (i & 3)) << 5);
+    };
+    auto sgt_s = [&](int i) { return sgt_s0 + (i >> 2) * 32u + (sgt_wl ^ (kWarps * (i & 3))); };
+    auto sg_g = [&](int i) { return sg_base + static_cast<uint64_t>(i) * sg_step; };
+    auto sg_s = [&](int i) { return (warp + kWarps * i) * 32u + lane; };
+    auto br_g = [&](int i) { return br_kb | (__brev(static_cast<uint32_t>(kWarps * i)) >> br_sh); };
+    auto br_s = [&](int i) { return (warp + kWarps * i) * 32u + col_r; };
 
     // ---------------------------------------------------------------- load
     uint32_t bad = 0;
-    if constexpr (ROLE == kTop) {
-        if (reads_user) {  // natural order, lanes = columns
+    const W one_q = static_cast<W>(lc.one_shoup);
 #pragma unroll 1
-            for (int i0 = 0; i0 < kPerThread; i0 += kBatch) {
-                uint64_t x[kBatch];
+    for (int i0 = 0; i0 < kPerThread; i0 += kBatch) {
+        if constexpr (ROLE == kTop) {
+            if (reads_user) {
+                unsigned long long x[kBatch];
 #pragma unroll
-                for (int i = 0; i < kBatch; ++i) {
-                    const uint32_t row = c.warp + kWarps * (i0 + i);
-                    x[i] = __ldcs(reinterpret_cast<const unsigned long long *>(a.in) + ubase + ((static_cast<int64_t>(row) << lo) | (c.t << 5) | c.lane));
-                }
+                for (int i = 0; i < kBatch; ++i) x[i] = __ldcs(uin + nat_g(i0 + i));
 #pragma unroll
-                for (int i = 0; i < kBatch; ++i) {
-                    const uint32_t row = c.warp + kWarps * (i0 + i);
-                    tile[tile_addr<S, ROLE>(row, c.lane)] =
-                        A::load_reduce(x[i], q, static_cast<W>(lc.one_shoup), bad);
-                }
-            }
-        } else {  // sigma order, lanes = the row's top five bits
-#pragma unroll 1
-            for (int i0 = 0; i0 < kPerThread; i0 += kBatch) {
+                for (int i = 0; i < kBatch; ++i) tile[nat_s(i0 + i)] = A::load_reduce(x[i], q, one_q, bad);
+            } else {
                 W x[kBatch];
 #pragma unroll
-                for (int i = 0; i < kBatch; ++i) {
-                    const uint32_t pr = c.warp + kWarps * (i0 + i), rlo = pr >> 5, col = pr & 31u;
-                    x[i] = __ldcs(sc + ((((static_cast<uint64_t>(rlo) << lo) | (c.t << 5) | col) << 5) | c.lane));
-                }
+                for (int i = 0; i < kBatch; ++i) x[i] = __ldcs(sc + sgt_g(i0 + i));
 #pragma unroll
-                for (int i = 0; i < kBatch; ++i) {
-                    const uint32_t pr = c.warp + kWarps * (i0 + i), rlo = pr >> 5, col = pr & 31u;
-                    tile[tile_addr<S, ROLE>((c.lane << (S - 5)) | rlo, col)] = x[i];
-                }
+                for (int i = 0; i < kBatch; ++i) tile[sgt_s(i0 + i)] = x[i];
             }
-        }
-    } else {
-        if (reads_user) {  // LOW, bit-reversed order: lane l takes column bitrev5(l)
-            const uint32_t col = __brev(c.lane) >> 27;
-#pragma unroll 1
-            for (int i0 = 0; i0 < kPerThread; i0 += kBatch) {
-                uint64_t x[kBatch];
+        } else {
+            if (reads_user) {
+                unsigned long long x[kBatch];
 #pragma unroll
-                for (int i = 0; i < kBatch; ++i) {
-                    const uint32_t row = c.warp + kWarps * (i0 + i);
-                    const uint32_t p = (col << (L - 5)) | (t_hi << S) | row;
-                    x[i] = __ldcs(reinterpret_cast<const unsigned long long *>(a.in) + ubase + (__brev(p) >> (32 - L)));
-                }
+                for (int i = 0; i < kBatch; ++i) x[i] = __ldcs(uin + br_g(i0 + i));
 #pragma unroll
-                for (int i = 0; i < kBatch; ++i) {
-                    const uint32_t row = c.warp + kWarps * (i0 + i);
-                    tile[tile_addr<S, ROLE>(row, col)] = A::load_reduce(x[i], q, static_cast<W>(lc.one_shoup), bad);
-                }
-            }
-        } else {  // sigma order, lanes = columns
-#pragma unroll 1
-            for (int i0 = 0; i0 < kPerThread; i0 += kBatch) {
+                for (int i = 0; i < kBatch; ++i) tile[br_s(i0 + i)] = A::load_reduce(x[i], q, one_q, bad);
+            } else {
                 W x[kBatch];
 #pragma unroll
-                for (int i = 0; i < kBatch; ++i) {
-                    const uint32_t row = c.warp + kWarps * (i0 + i);
-                    x[i] = __ldcs(sc + ((static_cast<uint64_t>((t_hi << (lo + S)) | (row << lo) | t_lo) << 5) | c.lane));
-                }
+                for (int i = 0; i < kBatch; ++i) x[i] = __ldcs(sc + sg_g(i0 + i));
 #pragma unroll
-                for (int i = 0; i < kBatch; ++i) {
-                    const uint32_t row = c.warp + kWarps * (i0 + i);
-                    tile[tile_addr<S, ROLE>(row, c.lane)] = x[i];
-                }
+                for (int i = 0; i < kBatch; ++i) tile[sg_s(i0 + i)] = x[i];
             }
         }
     }
@@ -275,43 +307,22 @@ __global__ void __launch_bounds__(kThreads) k_ntt_pass(KArgs a, typename A::W *s
     __syncthreads();
 
     // ----------------------------------------------------------- butterflies
-    rounds_from<A, GS, S, ROLE, 0>(tile, tw, lc, c);
+    rounds_from<A, GS, SCALE, S, ROLE, 0>(tile, tw, lc, c);
     __syncthreads();
 
     // --------------------------------------------------------------- store
-    if constexpr (ROLE == kTop) {
-        if (writes_user) {  // natural order, canonical residues
-#pragma unroll 4
-            for (int i = 0; i < kPerThread; ++i) {
-                const uint32_t row = c.warp + kWarps * i;
-                __stcs(reinterpret_cast<unsigned long long *>(a.out) + ubase + ((static_cast<int64_t>(row) << lo) | (c.t << 5) | c.lane),
-                       static_cast<unsigned long long>(A::canon(tile[tile_addr<S, ROLE>(row, c.lane)], q)));
-            }
+#pragma unroll 8
+    for (int i = 0; i < kPerThread; ++i) {
+        if constexpr (ROLE == kTop) {
+            if (writes_user)
+                __stcs(uout + nat_g(i), static_cast<unsigned long long>(A::canon(tile[nat_s(i)], q)));
+            else
+                __stcs(sc + sgt_g(i), tile[sgt_s(i)]);
         } else {
-#pragma unroll 4
-            for (int i = 0; i < kPerThread; ++i) {
-                const uint32_t pr = c.warp + kWarps * i, rlo = pr >> 5, col = pr & 31u;
-                __stcs(sc + ((((static_cast<uint64_t>(rlo) << lo) | (c.t << 5) | col) << 5) | c.lane),
-                       tile[tile_addr<S, ROLE>((c.lane << (S - 5)) | rlo, col)]);
-            }
-        }
-    } else {
-        if (writes_user) {  // LOW, bit-reversed order
-            const uint32_t col = __brev(c.lane) >> 27;
-#pragma unroll 4
-            for (int i = 0; i < kPerThread; ++i) {
-                const uint32_t row = c.warp + kWarps * i;
-                const uint32_t p = (col << (L - 5)) | (t_hi << S) | row;
-                __stcs(reinterpret_cast<unsigned long long *>(a.out) + ubase + (__brev(p) >> (32 - L)),
-                       static_cast<unsigned long long>(A::canon(tile[tile_addr<S, ROLE>(row, col)], q)));
-            }
-        } else {
-#pragma unroll 4
-            for (int i = 0; i < kPerThread; ++i) {
-                const uint32_t row = c.warp + kWarps * i;
-                __stcs(sc + ((static_cast<uint64_t>((t_hi << (lo + S)) | (row << lo) | t_lo) << 5) | c.lane),
-                       tile[tile_addr<S, ROLE>(row, c.lane)]);
-            }
+            if (writes_user)
+                __stcs(uout + br_g(i), static_cast<unsigned long long>(A::canon(tile[br_s(i)], q)));
+            else
+                __stcs(sc + sg_g(i), tile[sg_s(i)]);
         }
     }
 }
