@@ -16,6 +16,7 @@ namespace bc {
 // only ever stores the same flag value, so plain stores cannot lose a flag.
 enum : uint32_t {
     kStatusInputRange = 1u,  // a coefficient >= 2^32 reached a 32-bit-word plan
+    kStatusWaitTimeout = 2u,  // a bounded wait on an asynchronous copy ran out
 };
 
 #ifdef __CUDACC__

@@ -159,6 +159,47 @@ __device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+// One-thread bulk copies (TMA, non-tensor form) global -> shared, completed
+// through a transaction-counting mbarrier in shared memory.
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses (made
+// visible to it by a barrier) before its following bulk copies.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Arms the barrier's current phase for `bytes` and starts the copy; src and
+// dst 16-byte aligned, bytes a multiple of 16 below 2^20.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Waits for phase `parity` with an iteration limit (each try_wait suspends
+// the thread for a hardware-bounded time); false if the limit ran out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 22); ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
 // Twiddle chunks of one pass, in execution order.  Stage st of the pass
 // (CT: position bits high to low, GS: low to high) uses 2^k twiddles,
 // k = hi - b; they are fetched kCh at a time, each chunk `kAhead` chunks
@@ -291,7 +332,7 @@ struct Shape {
 // Shared memory of one CTA: the working array (padded, one word per
 // coefficient) and the staging buffer (the CTA's share of the next
 // polynomial as raw u64 words).
-template <class A, int L, int LOGE, bool PF>
+template <class A, int L, int LOGE, int PF>
 struct Smem {
     static constexpr uint32_t kLocal = Shape<L, LOGE>::kLocal;
     static constexpr uint32_t kWorkBytes = ((sizeof(typename A::W) * (kLocal + (kLocal >> 5) + (kLocal >> 10) + (kLocal >> 15)) + 127) / 128) * 128;
@@ -301,7 +342,7 @@ struct Smem {
 
 // CTAs per SM the launch bounds are sized for: as many as shared memory
 // (228 KB per SM, 1 KB reserved per CTA) and the 2048-thread limit allow.
-template <class A, int L, int LOGE, bool PF>
+template <class A, int L, int LOGE, int PF>
 struct Occupancy {
     static constexpr int kT = Shape<L, LOGE>::kT;
     static constexpr int kBySmem = static_cast<int>((228u * 1024u) / (Smem<A, L, LOGE, PF>::kBytes + 1024u));
@@ -649,9 +690,12 @@ struct Step {
 // c, c + G, c + 2G, ... (limb-major, so consecutive ones mostly share a
 // limb's twiddles).  While polynomial i is transformed, the copies of
 // polynomial i + G are already in flight into the staging buffer.
-// PF = false: one polynomial per cluster, grid = all polynomials, the CTA
+// PF = 1 issues those copies as 16-byte cp.async per thread; PF = 2 (one-CTA
+// schedules only) as one bulk copy (TMA) per polynomial from one thread,
+// completed through an mbarrier.
+// PF = 0: one polynomial per cluster, grid = all polynomials, the CTA
 // loads its share straight into the working array (more CTAs per SM).
-template <class A, int L, int LOGE, bool GS, bool SCALE, bool PF>
+template <class A, int L, int LOGE, bool GS, bool SCALE, int PF>
 __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, PF>::kMinBlocks)) k_ntt_fast(KArgs a) {
     using W = typename A::W;
     using Sh = Shape<L, LOGE>;
@@ -690,6 +734,45 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, PF>
         Out::store(work, a.out + base_of(cl), rank, lc);
         return;
     }
+    if constexpr (PF == 2) {
+        static_assert(Sh::kC == 1, "bulk-copy staging needs the whole polynomial in one CTA");
+        // One CTA holds the whole polynomial, so its share is the contiguous
+        // range [0, N) and staging element i is natural index i (Coop::convert
+        // reads it in that order).
+        __shared__ __align__(8) uint64_t bar;
+        constexpr uint32_t kBytes = 8u * Sh::kLocal;
+        if (threadIdx.x == 0) mbar_init(&bar, 1);
+        __syncthreads();
+        uint32_t parity = 0;
+        if (cl < npolys && threadIdx.x == 0) bulk_load(stage, a.in + base_of(cl), kBytes, &bar);
+        for (; cl < npolys; cl += G) {
+            const uint32_t limb = static_cast<uint32_t>(cl / a.batch);
+            const LimbConst &lc = a.limbs[limb];
+            const typename A::Tw *tw = reinterpret_cast<const typename A::Tw *>(a.tw) + (static_cast<size_t>(limb) << L);
+            const bool ok = mbar_wait_bounded(&bar, parity);
+            if (__syncthreads_or(!ok)) {  // a copy that never lands: report, drain once more, leave
+                if (threadIdx.x == 0) store_status(a.status, kStatusWaitTimeout);
+                mbar_wait_bounded(&bar, parity);
+                return;
+            }
+            parity ^= 1u;
+            In::convert(stage, work, rank, lc, bad);
+            __syncthreads();  // staging consumed by every thread
+            if (cl + G < npolys && threadIdx.x == 0) {
+                fence_proxy_async_smem();
+                bulk_load(stage, a.in + base_of(cl + G), kBytes, &bar);
+            }
+            typename First::Ring ring;
+            First::prefetch(ring, tw, rank);
+            First::run(work, tw, lc, rank, ring);
+            Out::store(work, a.out + base_of(cl), rank, lc);
+            __syncthreads();
+        }
+        if constexpr (A::kBits == 32) {
+            if (__any_sync(0xffffffffu, bad != 0) && (threadIdx.x & 31) == 0) store_status(a.status, kStatusInputRange);
+        }
+        return;
+    }
     if (cl < npolys) In::prefetch(stage, a.in + base_of(cl), rank);
     for (; cl < npolys; cl += G) {
         const uint32_t limb = static_cast<uint32_t>(cl / a.batch);
@@ -710,7 +793,7 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, PF>
     }
 }
 
-template <class A, int L, int LOGE, bool GS, bool SCALE, bool PF>
+template <class A, int L, int LOGE, bool GS, bool SCALE, int PF>
 int launch_one(const KArgs &a, cudaStream_t s) {
     using Sh = Shape<L, LOGE>;
     auto kern = k_ntt_fast<A, L, LOGE, GS, SCALE, PF>;
@@ -771,7 +854,7 @@ int launch_one(const KArgs &a, cudaStream_t s) {
 // C: every CTA reads its share of B^ before the cluster barrier of the
 // inverse's phase change, and writes C only after it.
 template <class A, int L, int LOGE>
-__global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, false>::kMinBlocks))
+__global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, 0>::kMinBlocks))
     k_polymul_fast(KArgs a) {
     using W = typename A::W;
     using Sh = Shape<L, LOGE>;
@@ -822,7 +905,7 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, fal
 // A^ and B^ (inverse) before the phase-change barrier that precedes every
 // store.
 template <class A, int L, int LOGE, bool INV>
-__global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, false>::kMinBlocks))
+__global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, 0>::kMinBlocks))
     k_ntt_mul_fast(KArgs a) {
     using W = typename A::W;
     using Sh = Shape<L, LOGE>;
@@ -859,7 +942,7 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, fal
 template <class A, int L, int LOGE>
 int launch_per_poly(void (*kern)(KArgs), bool *attr_set, const char *name, const KArgs &a, cudaStream_t s) {
     using Sh = Shape<L, LOGE>;
-    const size_t smem = Smem<A, L, LOGE, false>::kBytes;
+    const size_t smem = Smem<A, L, LOGE, 0>::kBytes;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !attr_set[dev]) {
@@ -899,7 +982,7 @@ template <class A, int L, int LOGE>
 int launch_polymul_one(const KArgs &a, cudaStream_t s) {
     using Sh = Shape<L, LOGE>;
     auto kern = k_polymul_fast<A, L, LOGE>;
-    const size_t smem = Smem<A, L, LOGE, false>::kBytes;
+    const size_t smem = Smem<A, L, LOGE, 0>::kBytes;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -931,25 +1014,33 @@ int launch_polymul_one(const KArgs &a, cudaStream_t s) {
 }
 
 // Persistent prefetching launches are not used by default: with their
-// staging buffers only two 512-thread CTAs fit an SM, and measured on
-// B200 that loses more to barrier and shared-memory-queue stalls than the
-// prefetch gains.  BARRACUDA_NTT_PERSISTENT=1 selects them.
-inline bool use_persistent() {
-    static const bool on = [] {
+// staging buffers fewer CTAs fit an SM, and measured on B200 that loses
+// more to barrier and shared-memory-queue stalls than the prefetch gains.
+// BARRACUDA_NTT_PERSISTENT=1 selects them with per-thread cp.async copies,
+// =2 with one bulk copy (TMA) per polynomial where one CTA holds the whole
+// polynomial (N <= 2^13), cp.async otherwise.
+inline int persistent_mode() {
+    static const int mode = [] {
         const char *e = std::getenv("BARRACUDA_NTT_PERSISTENT");
-        return e && e[0] == '1';
+        return e && (e[0] == '1' || e[0] == '2') ? e[0] - '0' : 0;
     }();
-    return on;
+    return mode;
+}
+
+template <class A, int L, int LOGE, int PF>
+int launch_dir(bool gs, bool scale, const KArgs &a, cudaStream_t s) {
+    if (gs) return scale ? launch_one<A, L, LOGE, true, true, PF>(a, s) : launch_one<A, L, LOGE, true, false, PF>(a, s);
+    return scale ? launch_one<A, L, LOGE, false, true, PF>(a, s) : launch_one<A, L, LOGE, false, false, PF>(a, s);
 }
 
 template <class A, int LOGE, int L>
 int dispatch_dir(bool gs, bool scale, const KArgs &a, cudaStream_t s) {
-    if (use_persistent()) {
-        if (gs) return scale ? launch_one<A, L, LOGE, true, true, true>(a, s) : launch_one<A, L, LOGE, true, false, true>(a, s);
-        return scale ? launch_one<A, L, LOGE, false, true, true>(a, s) : launch_one<A, L, LOGE, false, false, true>(a, s);
+    const int mode = persistent_mode();
+    if constexpr (Shape<L, LOGE>::kC == 1) {
+        if (mode == 2) return launch_dir<A, L, LOGE, 2>(gs, scale, a, s);
     }
-    if (gs) return scale ? launch_one<A, L, LOGE, true, true, false>(a, s) : launch_one<A, L, LOGE, true, false, false>(a, s);
-    return scale ? launch_one<A, L, LOGE, false, true, false>(a, s) : launch_one<A, L, LOGE, false, false, false>(a, s);
+    if (mode != 0) return launch_dir<A, L, LOGE, 1>(gs, scale, a, s);
+    return launch_dir<A, L, LOGE, 0>(gs, scale, a, s);
 }
 
 template <class A, int V, int L>

@@ -60,6 +60,8 @@ int ctx_sync(bc_ctx *ctx) {
             return fail(BC_ERR_INVALID_INPUT,
                         "coefficient >= 2^32 given to a transform whose moduli are below 2^31 "
                         "(inputs must be reduced; the reference is exact only below 2^32)");
+        if (st & kStatusWaitTimeout)
+            return fail(BC_ERR_EXECUTION, "a kernel gave up waiting for an asynchronous copy (results undefined)");
         return fail(BC_ERR_EXECUTION, format("kernel reported status 0x%x", st));
     }
     return BC_OK;
