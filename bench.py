@@ -667,6 +667,8 @@ KERNEL_CASES = {
     "sub_then_inverse": (16, 16, "k_coeff + k_ntt_fast", 24),
     "forward_large": (20, 4, "k_ntt_pass", 16),          # N = 2^20: three multi-pass launches
     "inverse_large": (20, 4, "k_ntt_pass", 16),
+    "forward_w64": (16, 16, "k_ntt_fast", 16, 60),       # 64-bit words (primes below 2^60)
+    "inverse_w64": (16, 16, "k_ntt_fast", 16, 60),
 }
 
 
@@ -678,7 +680,8 @@ def run_kernel_case(args):
     import barracuda_b200 as bc
 
     case = args.kernel_case
-    logn, limbs, kernel, bytes_per_word = KERNEL_CASES[case]
+    logn, limbs, kernel, bytes_per_word = KERNEL_CASES[case][:4]
+    bits = KERNEL_CASES[case][4] if len(KERNEL_CASES[case]) > 4 else 31
     torch.cuda.set_device(0)
     dev = bc.Device(0)
     stream = torch.cuda.Stream()
@@ -688,7 +691,7 @@ def run_kernel_case(args):
     n = 1 << logn
     words = 1 << 25
     batch = words // (n * limbs)
-    qs = bc.ntt_primes(31, n, limbs)
+    qs = bc.ntt_primes(bits, n, limbs)
     psis = [bc.negacyclic_root(q, n) for q in qs]
     if case.endswith("_cyclic"):
         plan = bc.NttPlan(dev, n, qs, [p * p % q for p, q in zip(psis, qs)], mode=bc.CYCLIC)
@@ -714,6 +717,8 @@ def run_kernel_case(args):
         "inverse": lambda: plan.inverse(a, c, batch, stream=sh),
         "forward_large": lambda: plan.forward(a, c, batch, stream=sh),
         "inverse_large": lambda: plan.inverse(a, c, batch, stream=sh),
+        "forward_w64": lambda: plan.forward(a, c, batch, stream=sh),
+        "inverse_w64": lambda: plan.inverse(a, c, batch, stream=sh),
         "forward_mul": lambda: plan.forward_mul(a, b, c, batch, stream=sh),
         "inverse_mul": lambda: plan.inverse_mul(a, b, c, batch, stream=sh),
         "forward_add": lambda: plan.forward_add(a, b, c, batch, stream=sh),
@@ -735,7 +740,7 @@ def run_kernel_case(args):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     gbs = words * bytes_per_word / (ms / 1000.0) / 1e9
-    print(json.dumps({"kernel_case": case, "kernel": kernel, "N": n, "limbs": limbs, "batch": batch,
+    print(json.dumps({"kernel_case": case, "kernel": kernel, "N": n, "bits": bits, "limbs": limbs, "batch": batch,
                       "words": words, "bytes_per_word": bytes_per_word, "ms": ms, "gb_per_s": gbs,
                       "frac": gbs / hbm, "peak_gbs": hbm, "peak_kind": peak_kind,
                       "launches_before_timed": args.warmup}), flush=True)
