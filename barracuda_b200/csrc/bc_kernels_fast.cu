@@ -51,6 +51,14 @@ int fast_variant(Word w, uint32_t logn, bool inverse) {
 
 int fast_variant_for(Word w, uint32_t logn, bool inverse) { return fast_variant(w, logn, inverse); }
 
+int cluster_policy() {
+    static const int pol = [] {
+        const int v = std::getenv("BARRACUDA_CLUSTER_POLICY") ? env_int("BARRACUDA_CLUSTER_POLICY") : 2;
+        return v >= 0 && v <= 2 ? v : 2;
+    }();
+    return pol;
+}
+
 uint64_t fast_table_index(uint32_t L, int V, uint64_t knat, int pair) {
     if (knat == 0) return 0;
     uint32_t s = 0;

@@ -793,20 +793,6 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, PF>
     }
 }
 
-// Cluster launches ask the hardware to load-balance a cluster's CTAs over
-// the SMs (cudaClusterSchedulingPolicyLoadBalancing).  Measured on B200 at
-// N = 2^16 (config 3): +2.8% against the default policy, which spreads
-// them; BARRACUDA_CLUSTER_POLICY=0|1|2 overrides (default / spread / load
-// balancing).
-inline int cluster_policy() {
-    static const int pol = [] {
-        const char *e = std::getenv("BARRACUDA_CLUSTER_POLICY");
-        const int v = e ? std::atoi(e) : 2;
-        return v >= 0 && v <= 2 ? v : 2;
-    }();
-    return pol;
-}
-
 // Launch attributes of a cluster launch of kC CTAs: the cluster shape and
 // the scheduling policy (none for kC = 1).
 inline int cluster_attrs(cudaLaunchAttribute (&attr)[2], int kC) {
