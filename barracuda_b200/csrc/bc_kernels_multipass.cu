@@ -48,10 +48,17 @@ template <class A, bool GS, bool SCALE, int S, int ROLE>
 int launch_pass(const KArgs &a, void *scratch, uint32_t lo, cudaStream_t s) {
     using W = typename A::W;
     const size_t smem = sizeof(W) * (32u << S);
-    static const cudaError_t attr = cudaFuncSetAttribute(mp::k_ntt_pass<A, GS, SCALE, S, ROLE>,
-                                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                         static_cast<int>(smem));
-    if (attr != cudaSuccess) return cuda_fail(attr, "multi-pass transform shared memory");
+    // the shared-memory attribute is set once per device (each device loads
+    // its own copy of the kernel)
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !attr_set[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(mp::k_ntt_pass<A, GS, SCALE, S, ROLE>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return cuda_fail(e, "multi-pass transform shared memory");
+        if (dev < 64) attr_set[dev] = true;
+    }
     const uint32_t tile_bits = ROLE == mp::kTop ? lo - 5 : a.logn - 5 - S;
     const uint64_t blocks = (static_cast<uint64_t>(a.batch) * a.n_limbs) << tile_bits;
     if (blocks > 0x7FFFFFFFull) return fail(BC_ERR_UNSUPPORTED, "batch too large for the multi-pass transform");
