@@ -7,7 +7,7 @@
 // bit.  One CTA holds a tile of 32 such sub-transforms (32 "columns" x 2^S
 // "rows") in shared memory; warps take the columns as lanes, so every
 // shared-memory access of a warp touches 32 distinct banks, and each pass's
-// butterflies run in register rounds of up to 3 bits (radix 8) between
+// butterflies run in register rounds of 2 to 4 bits (radix 4..16) between
 // barriers.
 //
 //   TOP pass  (bits [L - S, L)):  columns = position bits [0, 5)
@@ -60,7 +60,8 @@ __host__ __device__ constexpr int round_lo(int S, int WB, int r) {
 
 // CTAs per SM a pass is compiled for (register budget 65536 / (256 x this)):
 // as many as its tile allows in shared memory (228 KB per SM) where the
-// largest round still fits without spills (ptxas -v), fewer otherwise.
+// largest round still fits its registers, fewer otherwise.  ptxas -v shows
+// no spills except 8-24 bytes in the 32-bit S = 8 TOP pass.
 template <class A, int S>
 __host__ __device__ constexpr int min_blocks() {
     if constexpr (sizeof(typename A::W) == 4)
