@@ -580,6 +580,33 @@ def test_plan_multipass_matches_oracle(device, logn, bits, mode):
     plan.close()
 
 
+@pytest.mark.parametrize("logn,limbs,batch", [(18, 3, 3), (19, 1, 5)])
+def test_plan_multipass_reference_stage_structure(device, logn, limbs, batch):
+    """Cyclic plans whose root is not a primitive N-th root (psi^4, a
+    primitive N/2-th root): the outputs then depend on the reference's exact
+    stage structure, which the multi-pass kernels follow through the plan's
+    tables.  Forward and inverse against the restatement of the reference's
+    shaders (exact below 2^31), on every limb, with odd limb and batch counts."""
+    n = 1 << logn
+    qs = bc.ntt_primes(31, n, limbs)
+    roots = [pow(bc.negacyclic_root(q, n), 4, q) for q in qs]
+    plan = bc.NttPlan(device, n, qs, roots, mode=bc.CYCLIC)
+    assert plan.info["kernel_kind"] == 2
+    total = limbs * batch * n
+    src, dst, inv = (_alloc(device, total) for _ in range(3))
+    plan.fill_uniform(src, batch, seed=logn * 3 + limbs)
+    plan.forward(src, dst, batch)
+    plan.inverse(src, inv, batch)
+    device.synchronize()
+    x, X, Y = src.to_u64(), dst.to_u64(), inv.to_u64()
+    for l in range(limbs):
+        off = (l * batch + (l % batch)) * n
+        xs, q, w = x[off:off + n], qs[l], roots[l]
+        assert (X[off:off + n] == O.ref_ntt(xs, n, q, w)).all(), ("forward", l)
+        assert (Y[off:off + n] == O.ref_intt(xs, n, q, modinv(w, q))).all(), ("inverse", l)
+    plan.close()
+
+
 @pytest.mark.parametrize("logn,bits", [(18, 31), (20, 60), (21, 31)])
 def test_plan_multipass_layouts(device, logn, bits):
     """The multi-pass kernels take any layout: padded strides, limbs not
