@@ -669,6 +669,7 @@ KERNEL_CASES = {
     "inverse_large": (20, 4, "k_ntt_pass", 16),
     "forward_13": (13, 32, "k_ntt_fast", 16),            # one CTA per polynomial (TMA staging with
                                                          # BARRACUDA_NTT_PERSISTENT=2)
+    "inverse_13": (13, 32, "k_ntt_fast", 16),
     "forward_w64": (16, 16, "k_ntt_fast", 16, 60),       # 64-bit words (primes below 2^60)
     "inverse_w64": (16, 16, "k_ntt_fast", 16, 60),
 }
@@ -720,6 +721,7 @@ def run_kernel_case(args):
         "forward_large": lambda: plan.forward(a, c, batch, stream=sh),
         "inverse_large": lambda: plan.inverse(a, c, batch, stream=sh),
         "forward_13": lambda: plan.forward(a, c, batch, stream=sh),
+        "inverse_13": lambda: plan.inverse(a, c, batch, stream=sh),
         "forward_w64": lambda: plan.forward(a, c, batch, stream=sh),
         "inverse_w64": lambda: plan.inverse(a, c, batch, stream=sh),
         "forward_mul": lambda: plan.forward_mul(a, b, c, batch, stream=sh),
