@@ -18,6 +18,7 @@
 // on input loaded from natural index bitrev(p).
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cstdlib>
 
@@ -812,7 +813,7 @@ int launch_one(const KArgs &a, cudaStream_t s) {
     const size_t smem = Smem<A, L, LOGE, PF>::kBytes;
     // Per device: the shared-memory attribute, and how many clusters fit
     // at once (the persistent grid size).
-    static int resident[64] = {0};
+    static std::atomic<int> resident[64];  // zero-initialized; first calls may race harmlessly
     int dev = 0;
     cudaGetDevice(&dev);
     cudaLaunchConfig_t cfg = {};
@@ -822,7 +823,7 @@ int launch_one(const KArgs &a, cudaStream_t s) {
     cudaLaunchAttribute attr[2];
     cfg.attrs = attr;
     cfg.numAttrs = cluster_attrs(attr, Sh::kC);
-    int nres = dev < 64 ? resident[dev] : 0;
+    int nres = dev < 64 ? resident[dev].load() : 0;
     if (nres == 0) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return cuda_fail(e, "k_ntt_fast shared-memory attribute");
@@ -844,7 +845,7 @@ int launch_one(const KArgs &a, cudaStream_t s) {
         }
         if (nres <= 0)
             return fail(BC_ERR_UNSUPPORTED, format("k_ntt_fast<%d>: no cluster of %d CTAs fits an SM set", L, Sh::kC));
-        if (dev < 64) resident[dev] = nres;
+        if (dev < 64) resident[dev].store(nres);
     }
     const uint64_t polys = static_cast<uint64_t>(a.batch) * a.n_limbs;
     const uint64_t clusters = (!PF || polys < static_cast<uint64_t>(nres)) ? polys : static_cast<uint64_t>(nres);
@@ -948,19 +949,20 @@ __global__ void __launch_bounds__(Shape<L, LOGE>::kT, (Occupancy<A, L, LOGE, 0>:
 
 // One cluster of Shape<L, LOGE>::kC CTAs per (limb, polynomial).
 template <class A, int L, int LOGE>
-int launch_per_poly(void (*kern)(KArgs), bool *attr_set, const char *name, const KArgs &a, cudaStream_t s) {
+int launch_per_poly(void (*kern)(KArgs), std::atomic<bool> *attr_set, const char *name, const KArgs &a,
+                    cudaStream_t s) {
     using Sh = Shape<L, LOGE>;
     const size_t smem = Smem<A, L, LOGE, 0>::kBytes;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 64 || !attr_set[dev]) {
+    if (dev >= 64 || !attr_set[dev].load()) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return cuda_fail(e, format("%s shared-memory attribute", name).c_str());
         if (Sh::kC > 8) {
             e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
             if (e != cudaSuccess) return cuda_fail(e, format("%s cluster-size attribute", name).c_str());
         }
-        if (dev < 64) attr_set[dev] = true;
+        if (dev < 64) attr_set[dev].store(true);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(Sh::kT);
@@ -978,7 +980,7 @@ int launch_per_poly(void (*kern)(KArgs), bool *attr_set, const char *name, const
 
 template <class A, int L, int LOGE, bool INV>
 int launch_ntt_mul_one(const KArgs &a, cudaStream_t s) {
-    static bool attr_set[64] = {false};
+    static std::atomic<bool> attr_set[64];
     return launch_per_poly<A, L, LOGE>(k_ntt_mul_fast<A, L, LOGE, INV>, attr_set, "k_ntt_mul_fast", a, s);
 }
 
@@ -987,17 +989,17 @@ int launch_polymul_one(const KArgs &a, cudaStream_t s) {
     using Sh = Shape<L, LOGE>;
     auto kern = k_polymul_fast<A, L, LOGE>;
     const size_t smem = Smem<A, L, LOGE, 0>::kBytes;
-    static bool attr_set[64] = {false};
+    static std::atomic<bool> attr_set[64];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 64 || !attr_set[dev]) {
+    if (dev >= 64 || !attr_set[dev].load()) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return cuda_fail(e, "k_polymul_fast shared-memory attribute");
         if (Sh::kC > 8) {
             e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
             if (e != cudaSuccess) return cuda_fail(e, "k_polymul_fast cluster-size attribute");
         }
-        if (dev < 64) attr_set[dev] = true;
+        if (dev < 64) attr_set[dev].store(true);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(Sh::kT);

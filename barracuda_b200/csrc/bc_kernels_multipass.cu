@@ -1,5 +1,6 @@
 // bc_kernels_multipass.cu -- pass schedule, table layout and launches of the
 // multi-pass transform (kernels in bc_kernels_multipass.cuh).
+#include <atomic>
 #include <cstdint>
 
 #include "bc_common.hpp"
@@ -49,15 +50,15 @@ int launch_pass(const KArgs &a, void *scratch, uint32_t lo, cudaStream_t s) {
     using W = typename A::W;
     const size_t smem = sizeof(W) * (32u << S);
     // the shared-memory attribute is set once per device (each device loads
-    // its own copy of the kernel)
-    static bool attr_set[64] = {false};
+    // its own copy of the kernel); concurrent first calls only repeat it
+    static std::atomic<bool> attr_set[64];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 64 || !attr_set[dev]) {
+    if (dev >= 64 || !attr_set[dev].load()) {
         const cudaError_t e = cudaFuncSetAttribute(mp::k_ntt_pass<A, GS, SCALE, S, ROLE>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return cuda_fail(e, "multi-pass transform shared memory");
-        if (dev < 64) attr_set[dev] = true;
+        if (dev < 64) attr_set[dev].store(true);
     }
     const uint32_t tile_bits = ROLE == mp::kTop ? lo - 5 : a.logn - 5 - S;
     const uint64_t blocks = (static_cast<uint64_t>(a.batch) * a.n_limbs) << tile_bits;

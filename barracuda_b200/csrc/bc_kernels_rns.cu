@@ -3,6 +3,7 @@
 // coefficient-rescaling steps around the transforms.  All three are
 // HBM-bound: one read and one write per coefficient (decomposition writes
 // one word per digit).
+#include <atomic>
 #include <cstdint>
 #include <cstdlib>
 #include <string>
@@ -232,7 +233,7 @@ int launch_automorph_cluster(const KArgs &a, uint32_t galois, uint32_t ginv, con
                              uint64_t single_q, cudaStream_t s) {
     auto kern = k_automorph_cluster<LOGC, DIRECT>;
     constexpr size_t smem = (kClusterWords + 16) * sizeof(uint64_t);
-    static int resident[64] = {0};
+    static std::atomic<int> resident[64];
     int dev = 0;
     cudaGetDevice(&dev);
     cudaLaunchConfig_t cfg = {};
@@ -248,7 +249,7 @@ int launch_automorph_cluster(const KArgs &a, uint32_t galois, uint32_t ginv, con
     attr[1].val.clusterSchedulingPolicyPreference = static_cast<cudaClusterSchedulingPolicy>(cluster_policy());
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    int nres = dev < 64 ? resident[dev] : 0;
+    int nres = dev < 64 ? resident[dev].load() : 0;
     if (nres == 0) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return cuda_fail(e, "k_automorph_cluster shared-memory attribute");
@@ -261,7 +262,7 @@ int launch_automorph_cluster(const KArgs &a, uint32_t galois, uint32_t ginv, con
         if (e != cudaSuccess) return cuda_fail(e, "k_automorph_cluster occupancy");
         if (nres <= 0)
             return fail(BC_ERR_UNSUPPORTED, format("k_automorph_cluster: no cluster of %d CTAs fits", 1 << LOGC));
-        if (dev < 64) resident[dev] = nres;
+        if (dev < 64) resident[dev].store(nres);
     }
     const uint64_t polys = static_cast<uint64_t>(a.batch) * a.n_limbs;
     const uint64_t clusters = polys < static_cast<uint64_t>(nres) ? polys : static_cast<uint64_t>(nres);
