@@ -670,6 +670,8 @@ KERNEL_CASES = {
     "forward_13": (13, 32, "k_ntt_fast", 16),            # one CTA per polynomial (TMA staging with
                                                          # BARRACUDA_NTT_PERSISTENT=2)
     "inverse_13": (13, 32, "k_ntt_fast", 16),
+    "forward_512": (9, 64, "k_ntt_smem", 16),            # below the cluster kernels: one CTA, stage per barrier
+    "forward_unaligned": (16, 16, "k_glb_load + k_glb_stage + k_glb_store", 16),  # 8-byte aligned buffers
     "forward_w64": (16, 16, "k_ntt_fast", 16, 60),       # 64-bit words (primes below 2^60)
     "inverse_w64": (16, 16, "k_ntt_fast", 16, 60),
 }
@@ -700,10 +702,14 @@ def run_kernel_case(args):
         plan = bc.NttPlan(dev, n, qs, [p * p % q for p, q in zip(psis, qs)], mode=bc.CYCLIC)
     else:
         plan = bc.NttPlan(dev, n, qs, psis, mode=bc.NEGACYCLIC)
-    a = torch.empty(words, dtype=torch.int64, device="cuda")
+    # "_unaligned": operands start one word into their allocation (8-byte
+    # aligned only), which the cluster kernels do not take
+    off = 1 if case.endswith("_unaligned") else 0
+    a = torch.empty(words + 2 * off, dtype=torch.int64, device="cuda")
     b = torch.empty_like(a)
-    c = torch.empty(words * (3 if case == "decompose" else 1), dtype=torch.int64, device="cuda")
-    plan.fill_uniform(a, batch, seed=1, stream=sh)
+    c = torch.empty(words * (3 if case == "decompose" else 1) + 2 * off, dtype=torch.int64, device="cuda")
+    pa, pc = a.data_ptr() + 8 * off, c.data_ptr() + 8 * off
+    plan.fill_uniform(pa, batch, seed=1, stream=sh)
     plan.fill_uniform(b, batch, seed=2, stream=sh)
     ops = {
         "polymul": lambda: plan.polymul(a, b, c, batch, stream=sh),
@@ -722,6 +728,8 @@ def run_kernel_case(args):
         "inverse_large": lambda: plan.inverse(a, c, batch, stream=sh),
         "forward_13": lambda: plan.forward(a, c, batch, stream=sh),
         "inverse_13": lambda: plan.inverse(a, c, batch, stream=sh),
+        "forward_512": lambda: plan.forward(a, c, batch, stream=sh),
+        "forward_unaligned": lambda: plan.forward(pa, pc, batch, stream=sh),
         "forward_w64": lambda: plan.forward(a, c, batch, stream=sh),
         "inverse_w64": lambda: plan.inverse(a, c, batch, stream=sh),
         "forward_mul": lambda: plan.forward_mul(a, b, c, batch, stream=sh),
