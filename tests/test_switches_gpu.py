@@ -2,8 +2,8 @@
 process): each setting runs in a child process and must give the oracle's
 results.  The defaults are covered by every other GPU test; these are the
 non-default cluster scheduling policies, the selectable schedule variants of
-the N = 2^10..2^17 transforms and the automorphism kernels above the
-shared-memory size."""
+the N = 2^10..2^17 transforms (with the fused polynomial product on each)
+and the automorphism kernels above the shared-memory size."""
 import os
 import subprocess
 import sys
@@ -26,20 +26,24 @@ for logn, limbs, batch in {cases!r}:
     psis = [bc.negacyclic_root(q, n) for q in qs]
     plan = bc.NttPlan(dev, n, qs, psis, mode=bc.NEGACYCLIC)
     total = limbs * batch * n
-    src, dst, back, rot = (bc.FheTensor(dev, 2 * total) for _ in range(4))
+    src, dst, back, rot, other, prod = (bc.FheTensor(dev, 2 * total) for _ in range(6))
     plan.fill_uniform(src, batch, seed=logn + 11)
+    plan.fill_uniform(other, batch, seed=logn + 12)
     plan.forward(src, dst, batch)
     plan.inverse(dst, back, batch)
     plan.automorphism(src, rot, batch, 5 ** 3 % (2 * n))
+    plan.polymul(src, other, prod, batch)
     dev.synchronize()
-    x, X, R = src.to_u64(), dst.to_u64(), rot.to_u64()
+    x, X, R, Y, P = src.to_u64(), dst.to_u64(), rot.to_u64(), other.to_u64(), prod.to_u64()
     assert (back.to_u64() == x).all(), ("round trip", logn)
     for l in range(limbs):
         off = (l * batch + batch - 1) * n
-        xs = x[off:off + n]
+        xs, ys = x[off:off + n], Y[off:off + n]
         assert (X[off:off + n] == O.exact_negacyclic_ntt(xs, n, qs[l], psis[l])).all(), ("forward", logn, l)
         assert (R[off:off + n] == O.automorphism(xs, n, 5 ** 3 % (2 * n), qs[l])).all(), ("automorphism", logn, l)
-    for t in (src, dst, back, rot):
+        want = O.batch_polymul("ref_negacyclic", xs, ys, n, [qs[l]], [psis[l]])
+        assert (P[off:off + n] == want).all(), ("polymul", logn, l)
+    for t in (src, dst, back, rot, other, prod):
         t.free()
     plan.close()
 dev.close()
